@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""Benchmark of the batched slogpf / slogdet path on 1..8 B200s.
+
+Default workload: slogpf forward + VJP of logabs, float32,
+batch 4096 of skew-symmetric S = A - A^T, A 128x128 iid N(0,1), prec="tf32x3". One step
+is one pass over the batch: sign, logabs and the gradient S^-T/2 of sum(logabs) from one
+fused launch through the C ABI (fermix_slogpf_grad). Scaling is weak: each rank
+factorises its own batch, no collective on the data path; the timed region is bracketed
+by barriers and the max over ranks is reported.
+
+    python bench.py [--gpus N --steps K --warmup W]
+    python bench.py --impl reference ...   # the reference's CPU path (the oracle port)
+
+Prints one JSON line on rank 0.
+"""
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "slogdet/slogpf matrices/sec fwd & fwd+bwd at 1-8 B200; % of roofline"
+KERNEL = {"slogpf": "pf_fused_kernel", "slogdet": "lu_fused_kernel"}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="fermix_b200", choices=["fermix_b200", "reference"])
+    ap.add_argument("--op", default="slogpf", choices=["slogpf", "slogdet"])
+    ap.add_argument("--fwd-only", action="store_true", help="forward only (default: forward + VJP)")
+    ap.add_argument("--batch", type=int, default=4096, help="matrices per GPU")
+    ap.add_argument("--n", type=int, default=128)
+    ap.add_argument("--dtype", default="f32", choices=["f32", "f64", "c64", "c128"])
+    ap.add_argument("--prec", default="tf32x3", choices=["tf32x3", "ieee"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-sample", type=int, default=256, help="matrices in the CPU baseline sample")
+    ap.add_argument("--ref-step", type=int, default=16, help="matrices per step of the reference arm")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def workload_name(a):
+    what = "fwd" if a.fwd_only else "fwd+VJP(logabs)"
+    return f"{a.op} {what} {a.dtype} B={a.batch}/GPU n={a.n} prec={a.prec}"
+
+
+def flops_bytes(a):
+    """Algorithmic work per matrix (complex = 4 real flops per multiply-add pair)."""
+    n = a.n
+    s = {"f32": 4, "f64": 8, "c64": 8, "c128": 16}[a.dtype]
+    cx = 4 if a.dtype in ("c64", "c128") else 1
+    if a.op == "slogdet":
+        fl = (2.0 / 3.0 if a.fwd_only else 2.0) * n**3
+    else:
+        fl = (1.0 / 3.0 if a.fwd_only else 5.0 / 3.0) * n**3
+    by = (1 if a.fwd_only else 2) * n * n * s
+    return fl * cx, by
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profiles(a):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary
+    (a line 'traffic_bytes_per_launch: X' for this workload), else None."""
+    name = f"{KERNEL[a.op]}_{a.dtype}_n{a.n}_{'fwd' if a.fwd_only else 'fwdbwd'}.md"
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch_scaled:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# --------------------------------------------------------------- clocks sampler
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.idx),
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- CPU (oracle) timing
+def cpu_rate(a, count, threads):
+    """Matrices/s of the oracle (the numpy / LAPACK restatement of the reference's
+    generic path) on `count` matrices of the workload."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+
+    from oracle import fallback as F
+
+    gen = np.random.default_rng(a.seed + 12345)
+    npdt = {"f32": np.float32, "f64": np.float64, "c64": np.complex64, "c128": np.complex128}[a.dtype]
+    A = gen.standard_normal((count, a.n, a.n))
+    if a.dtype in ("c64", "c128"):
+        A = A + 1j * gen.standard_normal((count, a.n, a.n))
+    A = A.astype(npdt)
+    with threadpool_limits(limits=threads):
+        t0 = time.perf_counter()
+        if a.op == "slogpf":
+            S = A - np.swapaxes(A, -1, -2)
+            if a.fwd_only:
+                F.slogpf(S)
+            else:
+                F.slogpf(S), F.slogpf_grad(S)
+        else:
+            if a.fwd_only:
+                F.slogdet(A)
+            else:
+                F.lu_parts(A, True)
+        dt = time.perf_counter() - t0
+    return count / dt, dt
+
+
+def run_reference(a, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    # warm-up and timed steps, each a bounded sample of the workload
+    for _ in range(max(a.warmup, 0)):
+        cpu_rate(a, max(1, a.ref_step // 4), threads)
+    total_m, total_t = 0, 0.0
+    for _ in range(a.steps):
+        r, dt = cpu_rate(a, a.ref_step, threads)
+        total_m += a.ref_step
+        total_t += dt
+    v = total_m / total_t
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": v,
+        "unit": "matrices/s",
+        "n_gpus": a.gpus,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": 1e3 * total_t / a.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": a.dtype,
+        "data": "synthetic (seeded iid N(0,1))",
+        "config": {"workload": workload_name(a), "op": a.op, "batch_per_gpu": a.batch, "n": a.n, "prec": a.prec},
+        "cpu_baseline": {
+            "value": v,
+            "unit": "matrices/s",
+            "cores": threads,
+            "kind": "port",
+            "sample": f"{a.ref_step} matrices per step x {a.steps} steps of the same workload (numpy/LAPACK "
+                      "restatement of the reference's generic path; the reference itself needs jax, absent here)",
+        },
+        "e2e": {"value": v, "unit": "matrices/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU arm
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank)
+        return
+
+    import numpy as np
+    import torch
+
+    from fermix_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    L = _lib.lib()
+    tdt = {"f32": torch.float32, "f64": torch.float64, "c64": torch.complex64, "c128": torch.complex128}[a.dtype]
+    rdt = torch.float32 if a.dtype in ("f32", "c64") else torch.float64
+    kind = {"f32": 0, "f64": 1, "c64": 2, "c128": 3}[a.dtype]
+    prec = {"tf32x3": 1, "ieee": 2}[a.prec]
+    B, n = a.batch, a.n
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed + 1000 * rank)
+    A = torch.randn((B, n, n), generator=g, device=dev, dtype=tdt)
+    if a.op == "slogpf":
+        A = (A - A.transpose(-1, -2)).contiguous()
+    sign = torch.empty(B, dtype=tdt, device=dev)
+    logabs = torch.empty(B, dtype=rdt, device=dev)
+    G = None if a.fwd_only else torch.empty_like(A)
+    op = _lib.FX_OP_SLOGPF if a.op == "slogpf" else _lib.FX_OP_SLOGDET
+    wsb = L.fermix_workspace_bytes(op, kind, B, n, 0 if a.fwd_only else 1)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def call(X, Gout):
+        if a.op == "slogpf":
+            if a.fwd_only:
+                st = L.fermix_slogpf(sp, kind, prec, B, n, 1, X.data_ptr(), sign.data_ptr(), logabs.data_ptr(),
+                                     None, ws.data_ptr(), wsb)
+            else:
+                st = L.fermix_slogpf_grad(sp, kind, prec, B, n, 1, X.data_ptr(), None, 0, 0, sign.data_ptr(),
+                                          logabs.data_ptr(), None, Gout.data_ptr(), ws.data_ptr(), wsb)
+        else:
+            if a.fwd_only:
+                st = L.fermix_slogdet(sp, kind, prec, B, n, X.data_ptr(), sign.data_ptr(), logabs.data_ptr(), None,
+                                      ws.data_ptr(), wsb)
+            else:
+                st = L.fermix_slogdet_grad(sp, kind, prec, B, n, X.data_ptr(), None, 0, 0, sign.data_ptr(),
+                                           logabs.data_ptr(), None, Gout.data_ptr(), ws.data_ptr(), wsb)
+        _lib.check(st)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing
+    for _ in range(a.warmup):
+        call(A, G)
+    barrier()
+    clocks = Clocks(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                    os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+    clocks.start()
+    time.sleep(0.2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(a.steps):
+        call(A, G)
+    e1.record(stream)
+    barrier()
+    ck = clocks.stop()
+    t_dev = e0.elapsed_time(e1) / 1e3
+    t_dev = max_over_ranks(t_dev)
+    value = world * B * a.steps / t_dev
+    ms_step = 1e3 * t_dev / a.steps
+    fl, by = flops_bytes(a)
+    launch_s = t_dev / a.steps  # one launch per step
+    hbm, peak_kind = peaks()
+    achieved = B * by / launch_s / 1e9
+    roofline = {
+        "bound": "hbm",
+        "achieved": achieved,
+        "peak": hbm,
+        "unit": "GB/s",
+        "frac": achieved / hbm,
+        "traffic": traffic_from_profiles(a),
+        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+        "kernel": KERNEL[a.op],
+        "algorithmic_bytes_per_launch": B * by,
+        "flops_per_launch": B * fl,
+        "achieved_tflops": B * fl / launch_s / 1e12,
+    }
+
+    # ---- end to end through the C ABI with host buffers
+    e2e = None
+    if not a.no_e2e:
+        hA = torch.empty(A.shape, dtype=tdt, pin_memory=True)
+        hA.copy_(A)
+        dA = torch.empty_like(A)
+        hS = torch.empty(B, dtype=tdt, pin_memory=True)
+        hL = torch.empty(B, dtype=rdt, pin_memory=True)
+        hG = None if a.fwd_only else torch.empty(A.shape, dtype=tdt, pin_memory=True)
+        dG = None if a.fwd_only else torch.empty_like(A)
+        ke = max(3, min(a.steps, 20))
+
+        def e2e_step():
+            dA.copy_(hA, non_blocking=True)
+            call(dA, dG)
+            hS.copy_(sign, non_blocking=True)
+            hL.copy_(logabs, non_blocking=True)
+            if hG is not None:
+                hG.copy_(dG, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(ke):
+            e2e_step()
+        f1.record(stream)
+        barrier()
+        t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
+        h2d = A.numel() * A.element_size()
+        d2h = sign.numel() * sign.element_size() + logabs.numel() * logabs.element_size()
+        if hG is not None:
+            d2h += hG.numel() * hG.element_size()
+        e2e = {"value": world * B * ke / t_e2e, "unit": "matrices/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": ke}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        threads = os.cpu_count() or 1
+        r, dt = cpu_rate(a, a.cpu_sample, threads)
+        cpu = {"value": r, "unit": "matrices/s", "cores": threads, "kind": "port",
+               "sample": f"{a.cpu_sample} matrices of the same workload ({dt:.1f} s; numpy/LAPACK restatement of "
+                         "the reference's generic path, all host threads)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "matrices/s",
+            "n_gpus": world,
+            "steps": a.steps,
+            "warmup": a.warmup,
+            "ms_per_step": ms_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": a.dtype,
+            "data": "synthetic (seeded iid N(0,1), S = A - A^T)" if a.op == "slogpf" else "synthetic (seeded iid N(0,1))",
+            "config": {
+                "workload": workload_name(a),
+                "op": a.op,
+                "pass": "fwd" if a.fwd_only else "fwd+bwd",
+                "batch_per_gpu": B,
+                "n": n,
+                "prec": a.prec,
+                "parallelism": f"batch sharded x{world}, no collective",
+                "l2": "inputs exceed L2 (no flush needed)" if B * n * n * A.element_size() > 126e6 else "inputs fit L2",
+            },
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": a.steps,
+            "clocks": ck,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

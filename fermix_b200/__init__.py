@@ -1,0 +1,33 @@
+"""fermix_b200: batched determinants and Pfaffians (float32 / float64 / complex64 /
+complex128) on NVIDIA B200, with singular-safe gradients -- a drop-in for the public API
+of ChenAo-Phys/fermix (src/fermix/__init__.py:1-10) on torch CUDA tensors, computed by
+hand-written sm_100a kernels behind a C ABI (include/fermix_b200.h).
+
+Public functions: :func:`slogdet`, :func:`slogpf`, :func:`det`, :func:`pf`.
+"""
+
+from .api import (
+    FermixFallbackWarning,
+    det,
+    det_parts,
+    pf,
+    pf_parts,
+    slogdet,
+    slogdet_parts,
+    slogpf,
+    slogpf_parts,
+)
+
+__version__ = "0.1.0"
+__all__ = [
+    "slogdet",
+    "slogpf",
+    "det",
+    "pf",
+    "slogdet_parts",
+    "slogpf_parts",
+    "det_parts",
+    "pf_parts",
+    "FermixFallbackWarning",
+    "__version__",
+]

@@ -1,0 +1,400 @@
+"""Public API: slogdet, slogpf, det, pf -- the signatures, argument meanings, return
+dtypes and errors of ChenAo-Phys/fermix's ``src/fermix/api.py:148-227``, on torch CUDA
+tensors, computed by the hand-written sm_100a kernels of libfermix_b200.so.
+
+Differences from the reference, which is JAX-only:
+
+* inputs are torch tensors on a CUDA device (numpy arrays are copied to the current
+  CUDA device); a CPU tensor raises -- there is no CPU fallback, so
+  ``FermixFallbackWarning`` is exported for compatibility but never emitted;
+* derivatives go through torch autograd (``backward``, ``torch.autograd.grad``),
+  forward-mode AD (``torch.func.jvp`` via ``jvp``) and ``torch.func.vmap``. For complex
+  inputs torch's gradient convention is the conjugate of JAX's: where the reference's
+  ``jax.grad`` of ``sum(logabs)`` returns ``A^-T``, ``torch.autograd.grad`` returns
+  ``conj(A^-T)`` (the same convention as ``torch.linalg.slogdet``). Tangents (jvp) are
+  identical to the reference's.
+* ``slogdet_parts`` / ``slogpf_parts`` / ``det_parts`` / ``pf_parts`` return the
+  reference's (JAX-convention) derivative arrays directly -- the values of the reference's
+  ``jax.grad`` -- together with the forward, from one kernel launch.
+"""
+
+import numpy as np
+import torch
+
+from . import _lib
+
+_KIND = {
+    torch.float32: _lib.FX_F32,
+    torch.float64: _lib.FX_F64,
+    torch.complex64: _lib.FX_C64,
+    torch.complex128: _lib.FX_C128,
+}
+_PREC = {None: _lib.FX_PREC_DEFAULT, "tf32x3": _lib.FX_PREC_TF32X3, "ieee": _lib.FX_PREC_IEEE}
+
+
+class FermixFallbackWarning(UserWarning):
+    """Kept for API compatibility with the reference (src/fermix/api.py:19-21). This
+    build has no fallback path: non-CUDA inputs raise instead, so it is never emitted."""
+
+
+# ------------------------------------------------------------------ validation
+def _prep(a):
+    """dtype / shape checks of the reference's _prep (src/fermix/api.py:24-31)."""
+    from_host = False
+    if isinstance(a, np.ndarray):
+        a = torch.from_numpy(np.ascontiguousarray(a))
+        from_host = True
+    elif not isinstance(a, torch.Tensor):
+        a = torch.as_tensor(a)
+        from_host = True
+    if a.dtype not in _KIND:
+        raise TypeError(f"fermix supports float32, float64, complex64 and complex128, got {a.dtype}")
+    if a.ndim < 2 or a.shape[-1] != a.shape[-2]:
+        raise ValueError(f"expected (..., n, n), got {tuple(a.shape)}")
+    if a.device.type != "cuda":
+        if from_host and torch.cuda.is_available():
+            return a.cuda()  # like jnp.asarray: host data goes to the default device
+        raise RuntimeError(
+            f"fermix_b200 runs on CUDA devices only (got a tensor on {a.device}); "
+            "move it with .cuda() -- there is no CPU fallback"
+        )
+    return a
+
+
+def _check_block(block):
+    """src/fermix/api.py:92-97."""
+    if block is not None and block not in (32, 64, 128):
+        raise ValueError(f"block must be None, 32, 64 or 128, got {block!r}")
+    return block
+
+
+def _check_prec(dtype, prec):
+    """Field.check_prec (src/fermix/_field.py:265-275)."""
+    if prec not in _PREC:
+        raise ValueError(f"prec must be 'tf32x3' or 'ieee', got {prec!r}")
+    if prec == "tf32x3" and dtype in (torch.float64, torch.complex128):
+        raise ValueError(
+            "prec='tf32x3' applies to float32 / complex64 only; float64 and complex128 run "
+            "their block updates in IEEE fp64 (prec='ieee')"
+        )
+    return _PREC[prec]
+
+
+def _check_unroll(unroll_steps):
+    if unroll_steps is not None and not isinstance(unroll_steps, (bool, int)):
+        raise ValueError(f"unroll_steps must be None or a bool, got {unroll_steps!r}")
+
+
+def _check_upd_warps(upd_warps):
+    if upd_warps is not None and (not isinstance(upd_warps, int) or upd_warps < 1):
+        raise ValueError(f"upd_warps must be None or a positive int, got {upd_warps!r}")
+
+
+def _real(dtype):
+    return torch.float32 if dtype in (torch.float32, torch.complex64) else torch.float64
+
+
+# ------------------------------------------------------------------ library calls
+def _stream_ptr(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _workspace(op, kind, B, n, grad, dev):
+    nbytes = _lib.lib().fermix_workspace_bytes(op, kind, B, n, int(grad))
+    if nbytes == 0:
+        return None, 0
+    return torch.empty(nbytes, dtype=torch.uint8, device=dev), nbytes
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _run(op, A, prec, *, skew=True, grad=False, coef=None, conj_out=False, adjugate=False, value=False):
+    """One library call on the contiguous (B, n, n) CUDA tensor A: returns (sign,
+    logabs, value or None, grad or None)."""
+    L = _lib.lib()
+    B, n = A.shape[0], A.shape[-1]
+    kind = _KIND[A.dtype]
+    dev = A.device
+    sign = torch.empty(B, dtype=A.dtype, device=dev)
+    logabs = torch.empty(B, dtype=_real(A.dtype), device=dev)
+    val = torch.empty(B, dtype=A.dtype, device=dev) if value else None
+    G = torch.empty_like(A) if grad else None
+    if coef is not None:
+        coef = coef.to(dtype=A.dtype, device=dev).contiguous()
+    with torch.cuda.device(dev):
+        ws, wsb = _workspace(op, kind, B, n, grad, dev)
+        s = _stream_ptr(dev)
+        if op == _lib.FX_OP_SLOGDET:
+            if grad:
+                st = L.fermix_slogdet_grad(s, kind, prec, B, n, _ptr(A), _ptr(coef), int(conj_out), int(adjugate),
+                                           _ptr(sign), _ptr(logabs), _ptr(val), _ptr(G), _ptr(ws), wsb)
+            else:
+                st = L.fermix_slogdet(s, kind, prec, B, n, _ptr(A), _ptr(sign), _ptr(logabs), _ptr(val), _ptr(ws), wsb)
+        else:
+            if grad:
+                st = L.fermix_slogpf_grad(s, kind, prec, B, n, int(skew), _ptr(A), _ptr(coef), int(conj_out),
+                                          int(adjugate), _ptr(sign), _ptr(logabs), _ptr(val), _ptr(G), _ptr(ws), wsb)
+            else:
+                st = L.fermix_slogpf(s, kind, prec, B, n, int(skew), _ptr(A), _ptr(sign), _ptr(logabs), _ptr(val),
+                                     _ptr(ws), wsb)
+    _lib.check(st)
+    return sign, logabs, val, G
+
+
+def _flat(a):
+    batch = tuple(a.shape[:-2])
+    n = a.shape[-1]
+    B = int(np.prod(batch)) if batch else 1
+    return a.reshape(B, n, n).contiguous(), batch, n
+
+
+def _slog_coef(sign, g_sign, g_logabs, cplx):
+    """Per-matrix coefficient c with torch grad = conj(c * D), D the holomorphic
+    derivative of logabs: c = g_logabs + i Im(conj(g_sign) sign) (complex), g_logabs
+    (real). The sign's tangent is i Im(tr) sign (src/fermix/_diff.py:92-97)."""
+    if g_logabs is None:
+        g_logabs = torch.zeros(sign.shape, dtype=_real(sign.dtype), device=sign.device)
+    if not cplx:
+        return g_logabs
+    c = g_logabs.to(sign.dtype)
+    if g_sign is not None:
+        q = torch.imag(torch.conj(g_sign) * sign)
+        c = c + 1j * q.to(sign.dtype)
+    return c
+
+
+# ------------------------------------------------------------------ autograd
+def _fold(A, in_dim):
+    """vmap helper: move the vmapped axis first and fold it into the batch."""
+    A = A.movedim(in_dim, 0)
+    V, rest, n = A.shape[0], tuple(A.shape[1:-2]), A.shape[-1]
+    return A.reshape((-1, n, n)).contiguous(), V, rest
+
+
+class _FwdKernel(torch.autograd.Function):
+    """Non-differentiable forward launch: (sign, logabs, value) of a (B, n, n) batch."""
+
+    @staticmethod
+    def forward(A, op, prec, skew):
+        sign, logabs, val, _ = _run(op, A, prec, skew=skew, value=True)
+        return sign, logabs, val
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        ctx.mark_non_differentiable(*output)
+
+    @staticmethod
+    def vmap(info, in_dims, A, op, prec, skew):
+        if in_dims[0] is None:
+            return _FwdKernel.apply(A, op, prec, skew), (None, None, None)
+        X, V, rest = _fold(A, in_dims[0])
+        out = _FwdKernel.apply(X, op, prec, skew)
+        return tuple(o.reshape((V,) + rest) for o in out), (0, 0, 0)
+
+
+class _GradKernel(torch.autograd.Function):
+    """Non-differentiable gradient launch: G = coef * D (conjugated if conj_out) with D
+    the derivative matrix of the op (A^-T, adj(A)^T, S^-T/2 or pf S^-T/2)."""
+
+    @staticmethod
+    def forward(A, coef, op, prec, skew, conj_out, adjugate):
+        _, _, _, G = _run(op, A, prec, skew=skew, grad=True, coef=coef, conj_out=conj_out, adjugate=adjugate)
+        return G
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        ctx.mark_non_differentiable(output)
+
+    @staticmethod
+    def vmap(info, in_dims, A, coef, op, prec, skew, conj_out, adjugate):
+        da, dc = in_dims[0], in_dims[1]
+        if da is None and dc is None:
+            return _GradKernel.apply(A, coef, op, prec, skew, conj_out, adjugate), None
+        V = info.batch_size
+        if da is None:
+            A = A.unsqueeze(0).expand((V,) + tuple(A.shape))
+            da = 0
+        X, V, rest = _fold(A, da)
+        if coef is not None:
+            c = coef.movedim(dc, 0) if dc is not None else coef.unsqueeze(0).expand((V,) + tuple(coef.shape))
+            c = c.reshape(-1).contiguous()
+        else:
+            c = None
+        G = _GradKernel.apply(X, c, op, prec, skew, conj_out, adjugate)
+        n = X.shape[-1]
+        return G.reshape((V,) + rest + (n, n)), 0
+
+
+class _Slog(torch.autograd.Function):
+    """(sign, logabs) of slogdet (op=SLOGDET) or slogpf (op=SLOGPF) on a (B, n, n)
+    batch. Backward re-runs the factorisation with the gradient epilogue (one fused
+    launch writing the scaled gradient), so no (B, n, n) residual is kept; the primal it
+    recomputes is bit-identical to the forward's."""
+
+    @staticmethod
+    def forward(A, op, prec, skew):
+        sign, logabs, _ = _FwdKernel.apply(A, op, prec, skew)
+        return sign, logabs
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        A, op, prec, skew = inputs
+        ctx.save_for_backward(A, output[0])
+        ctx.save_for_forward(A, output[0])
+        ctx.op, ctx.prec, ctx.skew = op, prec, skew
+
+    @staticmethod
+    def backward(ctx, g_sign, g_logabs):
+        A, sign = ctx.saved_tensors
+        c = _slog_coef(sign, g_sign, g_logabs, A.is_complex())
+        G = _GradKernel.apply(A, c, ctx.op, ctx.prec, ctx.skew, True, False)
+        return G, None, None, None
+
+    @staticmethod
+    def jvp(ctx, dA, *_):
+        A, sign = ctx.saved_tensors
+        D = _GradKernel.apply(A, None, ctx.op, ctx.prec, ctx.skew, False, False)
+        t = (D * dA).sum(dim=(-1, -2))
+        if A.is_complex():
+            return (1j * t.imag).to(sign.dtype) * sign, t.real
+        return torch.zeros_like(sign), t
+
+    @staticmethod
+    def vmap(info, in_dims, A, op, prec, skew):
+        if in_dims[0] is None:
+            return _Slog.apply(A, op, prec, skew), (None, None)
+        X, V, rest = _fold(A, in_dims[0])
+        out = _Slog.apply(X, op, prec, skew)
+        return tuple(o.reshape((V,) + rest) for o in out), (0, 0)
+
+
+class _Value(torch.autograd.Function):
+    """det (op=SLOGDET) or pf (op=SLOGPF) value on a (B, n, n) batch, with the
+    singular-safe adjugate gradient."""
+
+    @staticmethod
+    def forward(A, op, prec, skew):
+        return _FwdKernel.apply(A, op, prec, skew)[2]
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        A, op, prec, skew = inputs
+        ctx.save_for_backward(A)
+        ctx.save_for_forward(A)
+        ctx.op, ctx.prec, ctx.skew = op, prec, skew
+
+    @staticmethod
+    def backward(ctx, g):
+        (A,) = ctx.saved_tensors
+        c = torch.conj(g) if A.is_complex() else g
+        G = _GradKernel.apply(A, c, ctx.op, ctx.prec, ctx.skew, True, True)
+        return G, None, None, None
+
+    @staticmethod
+    def jvp(ctx, dA, *_):
+        (A,) = ctx.saved_tensors
+        D = _GradKernel.apply(A, None, ctx.op, ctx.prec, ctx.skew, False, True)
+        return (D * dA).sum(dim=(-1, -2))
+
+    @staticmethod
+    def vmap(info, in_dims, A, op, prec, skew):
+        if in_dims[0] is None:
+            return _Value.apply(A, op, prec, skew), None
+        X, V, rest = _fold(A, in_dims[0])
+        return _Value.apply(X, op, prec, skew).reshape((V,) + rest), 0
+
+
+# ------------------------------------------------------------------ public functions
+def slogdet(a, *, prec=None, unroll_steps=None, block=None):
+    """Sign and log|det| of a batch of matrices ``a`` of shape (..., n, n)
+    (src/fermix/api.py:148-174). Returns (sign, logabsdet): sign has the dtype of ``a``
+    (exactly +-1 / 0 for real dtypes, a unit complex number for complex ones),
+    logabsdet the corresponding real dtype -- the conventions of
+    ``jnp.linalg.slogdet``. Exactly singular matrices give (0, -inf) and a zero
+    gradient. ``prec`` ("tf32x3" | "ieee"; "tf32x3" only for float32 / complex64) is
+    validated as in the reference; the block updates of this build run exact IEEE FMA
+    for every dtype, which is at least as accurate as either. ``block`` (None, 32, 64,
+    128) and ``unroll_steps`` are validated launch hints."""
+    a = _prep(a)
+    _check_block(block)
+    _check_unroll(unroll_steps)
+    p = _check_prec(a.dtype, prec)
+    A, batch, n = _flat(a)
+    sign, logabs = _Slog.apply(A, _lib.FX_OP_SLOGDET, p, True)
+    return sign.reshape(batch), logabs.reshape(batch)
+
+
+def slogpf(a, *, prec=None, skew_symmetrize=True, upd_warps=None):
+    """Sign and log|pf| of a batch of skew-symmetric matrices (S^T = -S, also for
+    complex dtypes; odd n gives (0, -inf)) (src/fermix/api.py:177-193). The input is
+    skew-symmetrised as (a - a^T)/2 unless ``skew_symmetrize=False`` (then it must be
+    exactly skew-symmetric). Gradient: S^-T / 2 (skew), zero for an exactly singular S."""
+    a = _prep(a)
+    _check_upd_warps(upd_warps)
+    p = _check_prec(a.dtype, prec)
+    A, batch, n = _flat(a)
+    sign, logabs = _Slog.apply(A, _lib.FX_OP_SLOGPF, p, bool(skew_symmetrize))
+    return sign.reshape(batch), logabs.reshape(batch)
+
+
+def det(a, *, prec=None, unroll_steps=None, block=None):
+    """Determinant of a batch of matrices (src/fermix/api.py:196-212); differentiable
+    with d det = tr(adj(A) dA), finite and exact for singular A of rank n-1 (up to two
+    exact zero pivots) and zero for rank <= n-2."""
+    a = _prep(a)
+    _check_block(block)
+    _check_unroll(unroll_steps)
+    p = _check_prec(a.dtype, prec)
+    A, batch, n = _flat(a)
+    return _Value.apply(A, _lib.FX_OP_SLOGDET, p, True).reshape(batch)
+
+
+def pf(a, *, prec=None, skew_symmetrize=True, upd_warps=None):
+    """Pfaffian of a batch of skew-symmetric matrices (src/fermix/api.py:215-227); odd n
+    gives 0. Differentiable with d pf = sum(G dS), G = pf S^-T / 2 continued to singular
+    S (rank n-2: the rank-2 Pfaffian adjugate; rank <= n-4: 0)."""
+    a = _prep(a)
+    _check_upd_warps(upd_warps)
+    p = _check_prec(a.dtype, prec)
+    A, batch, n = _flat(a)
+    return _Value.apply(A, _lib.FX_OP_SLOGPF, p, bool(skew_symmetrize)).reshape(batch)
+
+
+# ------------------------------------------------------------------ one-launch parts
+def _parts(op, a, prec, skew, adjugate, coef):
+    a = _prep(a)
+    p = _check_prec(a.dtype, prec)
+    A, batch, n = _flat(a)
+    if coef is not None:
+        coef = torch.as_tensor(coef, device=A.device).reshape(-1)
+    sign, logabs, val, G = _run(op, A, p, skew=skew, grad=True, coef=coef, adjugate=adjugate, value=adjugate)
+    shape = batch + (n, n)
+    if adjugate:
+        return val.reshape(batch), G.reshape(shape)
+    return sign.reshape(batch), logabs.reshape(batch), G.reshape(shape)
+
+
+def slogdet_parts(a, *, prec=None, coef=None):
+    """(sign, logabs, G) from one launch, G = coef * A^-T (the reference's jax.grad of
+    sum(logabs); zero for exactly singular members)."""
+    return _parts(_lib.FX_OP_SLOGDET, a, prec, True, False, coef)
+
+
+def slogpf_parts(a, *, prec=None, skew_symmetrize=True, coef=None):
+    """(sign, logabs, G) from one launch, G = coef * S^-T / 2 (the reference's jax.grad
+    of sum(logabs) w.r.t. a)."""
+    return _parts(_lib.FX_OP_SLOGPF, a, prec, skew_symmetrize, False, coef)
+
+
+def det_parts(a, *, prec=None, coef=None):
+    """(det, G) from one launch, G = coef * adj(A)^T (the reference's jax.grad of
+    sum(Re det))."""
+    return _parts(_lib.FX_OP_SLOGDET, a, prec, True, True, coef)
+
+
+def pf_parts(a, *, prec=None, skew_symmetrize=True, coef=None):
+    """(pf, G) from one launch, G = coef * pf(S) S^-T / 2 (the reference's jax.grad of
+    sum(Re pf))."""
+    return _parts(_lib.FX_OP_SLOGPF, a, prec, skew_symmetrize, True, coef)

@@ -1,0 +1,293 @@
+// extern "C" entry points of libfermix_b200.so (declared in include/fermix_b200.h).
+//
+// Dispatch (replacing the reference's per-GPU TUNES table, src/fermix/_common.py:17-378):
+//   det n <= 4, pf n <= 6      -> the closed forms (poly.cuh), one thread per matrix
+//   pf with odd n              -> (0, -inf), zero gradient
+//   otherwise                  -> the fused one-block-per-matrix kernels (fused_lu.cuh,
+//                                 fused_pf.cuh): work buffers in shared memory when
+//                                 they fit (227 KB per block on B200), else in the
+//                                 caller's workspace (one slot per resident block).
+// The only process state is a once-initialised per-device attribute cache.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "fermix_b200.h"
+#include "fused_pf.cuh"
+#include "poly.cuh"
+
+namespace {
+
+using namespace fx;
+
+constexpr int kMaxDevices = 64;
+
+struct DevInfo {
+  int sms = 0;
+  int smem_optin = 0;
+  int ok = 0;
+};
+
+DevInfo g_dev[kMaxDevices];
+std::once_flag g_once[kMaxDevices];
+
+const DevInfo* dev_info() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::call_once(g_once[dev], [dev]() {
+    DevInfo d;
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess)
+      d.ok = 1;
+    g_dev[dev] = d;
+  });
+  return g_dev[dev].ok ? &g_dev[dev] : nullptr;
+}
+
+int validate(int dtype, int prec, int64_t batch, int64_t n) {
+  if (dtype < FX_F32 || dtype > FX_C128) return FX_ERR_DTYPE;
+  if (batch < 0 || n < 0 || n > 46000) return FX_ERR_SHAPE;
+  return fermix_check_prec(dtype, prec);
+}
+
+int threads_for(int n) { return n <= 24 ? 32 : (n <= 64 ? 128 : 256); }
+
+// Launch geometry of one fused call (shared by the launch and the workspace query).
+template <typename T>
+struct Plan {
+  int threads = 0, ld = 0, in_smem = 0;
+  size_t smem = 0, slot = 0;
+  int64_t grid = 0;
+};
+
+template <typename T, bool PF>
+void* fused_kernel_ptr() {
+  return PF ? reinterpret_cast<void*>(&pf_fused_kernel<T>) : reinterpret_cast<void*>(&lu_fused_kernel<T>);
+}
+
+template <typename T, bool PF>
+int plan_fused(int64_t batch, int n, int mode, Plan<T>& P) {
+  const DevInfo* D = dev_info();
+  if (!D) return FX_ERR_DEVICE;
+  const int nbuf = mode == MODE_FWD ? 1 : 2;
+  P.threads = threads_for(n);
+  const int ld_s = (n % 2 == 0) ? n + 1 : n;  // odd stride: conflict-free column access
+  const size_t full = SmemLayout<T>::bytes(n, ld_s, nbuf, true);
+  P.in_smem = full <= (size_t)D->smem_optin;
+  P.ld = P.in_smem ? ld_s : n;
+  P.smem = P.in_smem ? full : SmemLayout<T>::bytes(n, n, nbuf, false);
+  P.slot = P.in_smem ? 0 : (size_t)nbuf * n * n * sizeof(T);
+  void* k = fused_kernel_ptr<T, PF>();
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem) != cudaSuccess)
+    return FX_ERR_CUDA;
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, P.threads, P.smem) != cudaSuccess) return FX_ERR_CUDA;
+  if (occ < 1) occ = 1;
+  P.grid = batch < (int64_t)D->sms * occ ? batch : (int64_t)D->sms * occ;
+  return FX_OK;
+}
+
+template <typename T, bool PF>
+int launch_fused(cudaStream_t s, Job<T> J, void* ws, size_t ws_bytes) {
+  Plan<T> P;
+  int e = plan_fused<T, PF>(J.B, J.n, J.mode, P);
+  if (e) return e;
+  J.ld = P.ld;
+  J.in_smem = P.in_smem;
+  J.ws = nullptr;
+  int64_t grid = P.grid;
+  if (!P.in_smem) {
+    if (!ws) return FX_ERR_WORKSPACE;
+    int64_t slots = (int64_t)(ws_bytes / P.slot);
+    if (slots < 1) return FX_ERR_WORKSPACE;
+    if (grid > slots) grid = slots;
+    J.ws = static_cast<T*>(ws);
+  }
+  if (grid < 1) return FX_OK;
+  if (PF)
+    pf_fused_kernel<T><<<(unsigned)grid, P.threads, P.smem, s>>>(J);
+  else
+    lu_fused_kernel<T><<<(unsigned)grid, P.threads, P.smem, s>>>(J);
+  return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+}
+
+template <typename T>
+int launch_poly(cudaStream_t s, const Job<T>& J, int is_pf) {
+  const int th = 128;
+  const int64_t blocks = (J.B + th - 1) / th;
+  poly_kernel<T><<<(unsigned)blocks, th, 0, s>>>(J, is_pf);
+  return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+}
+
+template <typename T>
+Job<T> make_job(int64_t batch, int64_t n, const void* a, const void* coef, int conj_out, int skew, int mode,
+                void* sign, void* logabs, void* value, void* grad) {
+  Job<T> J{};
+  J.a = static_cast<const T*>(a);
+  J.sign = static_cast<T*>(sign);
+  J.logabs = static_cast<typename Sc<T>::R*>(logabs);
+  J.g = static_cast<T*>(grad);
+  J.value = static_cast<T*>(value);
+  J.coef = static_cast<const T*>(coef);
+  J.conj_out = conj_out;
+  J.skew = skew;
+  J.B = batch;
+  J.n = (int)n;
+  J.mode = mode;
+  return J;
+}
+
+template <typename T>
+int run_det(cudaStream_t s, int64_t batch, int64_t n, const void* a, const void* coef, int conj_out, int mode,
+            void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb) {
+  Job<T> J = make_job<T>(batch, n, a, coef, conj_out, 0, mode, sign, logabs, value, grad);
+  if (n <= DET_POLY_MAX) return launch_poly<T>(s, J, 0);
+  return launch_fused<T, false>(s, J, ws, wsb);
+}
+
+template <typename T>
+int run_pf(cudaStream_t s, int64_t batch, int64_t n, int skew, const void* a, const void* coef, int conj_out,
+           int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb) {
+  Job<T> J = make_job<T>(batch, n, a, coef, conj_out, skew, mode, sign, logabs, value, grad);
+  if (n % 2 == 1) {
+    if (grad && batch * n * n > 0 &&
+        cudaMemsetAsync(grad, 0, (size_t)batch * n * n * sizeof(T), s) != cudaSuccess)
+      return FX_ERR_CUDA;
+    const int th = 128;
+    pf_odd_kernel<T><<<(unsigned)((batch + th - 1) / th), th, 0, s>>>(J);
+    return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+  }
+  if (n <= PF_POLY_MAX) return launch_poly<T>(s, J, 1);
+  return launch_fused<T, true>(s, J, ws, wsb);
+}
+
+template <typename F>
+int by_dtype(int dtype, F&& f) {
+  switch (dtype) {
+    case FX_F32:
+      return f(float());
+    case FX_F64:
+      return f(double());
+    case FX_C64:
+      return f(c64_t());
+    case FX_C128:
+      return f(c128_t());
+  }
+  return FX_ERR_DTYPE;
+}
+
+template <typename T>
+size_t ws_bytes_t(int op, int64_t batch, int64_t n, int grad) {
+  const int mode = grad ? MODE_SLOG_GRAD : MODE_FWD;
+  if (op == FX_OP_SLOGDET && n <= DET_POLY_MAX) return 0;
+  if (op == FX_OP_SLOGPF && (n % 2 == 1 || n <= PF_POLY_MAX)) return 0;
+  Plan<T> P;
+  int e = op == FX_OP_SLOGPF ? plan_fused<T, true>(batch, (int)n, mode, P) : plan_fused<T, false>(batch, (int)n, mode, P);
+  if (e || P.in_smem) return 0;
+  return (size_t)P.grid * P.slot;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fermix_check_prec(int dtype, int prec) {
+  if (prec != FX_PREC_DEFAULT && prec != FX_PREC_TF32X3 && prec != FX_PREC_IEEE) return FX_ERR_PREC;
+  if (prec == FX_PREC_TF32X3 && (dtype == FX_F64 || dtype == FX_C128)) return FX_ERR_PREC;
+  return FX_OK;
+}
+
+int fermix_slogdet(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a, void* sign,
+                   void* logabs, void* value, void* workspace, size_t workspace_bytes) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (batch == 0) return FX_OK;
+  if ((!a && n > 0) || !sign || !logabs) return FX_ERR_NULL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_det<T>(s, batch, n, a, nullptr, 0, MODE_FWD, sign, logabs, value, nullptr, workspace,
+                      workspace_bytes);
+  });
+}
+
+int fermix_slogdet_grad(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a,
+                        const void* coef, int conj_out, int adjugate, void* sign, void* logabs, void* value,
+                        void* grad, void* workspace, size_t workspace_bytes) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (batch == 0) return FX_OK;
+  if ((!a && n > 0) || !sign || !logabs || (!grad && n > 0)) return FX_ERR_NULL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_det<T>(s, batch, n, a, coef, conj_out, mode, sign, logabs, value, grad, workspace, workspace_bytes);
+  });
+}
+
+int fermix_slogpf(void* stream, int dtype, int prec, int64_t batch, int64_t n, int skew_symmetrize, const void* a,
+                  void* sign, void* logabs, void* value, void* workspace, size_t workspace_bytes) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (batch == 0) return FX_OK;
+  if ((!a && n > 0) || !sign || !logabs) return FX_ERR_NULL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_pf<T>(s, batch, n, skew_symmetrize, a, nullptr, 0, MODE_FWD, sign, logabs, value, nullptr, workspace,
+                     workspace_bytes);
+  });
+}
+
+int fermix_slogpf_grad(void* stream, int dtype, int prec, int64_t batch, int64_t n, int skew_symmetrize,
+                       const void* a, const void* coef, int conj_out, int adjugate, void* sign, void* logabs,
+                       void* value, void* grad, void* workspace, size_t workspace_bytes) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (batch == 0) return FX_OK;
+  if ((!a && n > 0) || !sign || !logabs || (!grad && n > 0)) return FX_ERR_NULL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_pf<T>(s, batch, n, skew_symmetrize, a, coef, conj_out, mode, sign, logabs, value, grad, workspace,
+                     workspace_bytes);
+  });
+}
+
+size_t fermix_workspace_bytes(int op, int dtype, int64_t batch, int64_t n, int grad) {
+  if (validate(dtype, FX_PREC_DEFAULT, batch, n) || batch == 0) return 0;
+  return (size_t)by_dtype(dtype, [&](auto t) -> int {
+    using T = decltype(t);
+    size_t b = ws_bytes_t<T>(op, batch, n, grad);
+    // returned through an int-typed dispatcher: report in 256-byte units
+    return (int)((b + 255) / 256);
+  }) * 256;
+}
+
+const char* fermix_strerror(int code) {
+  switch (code) {
+    case FX_OK:
+      return "ok";
+    case FX_ERR_DTYPE:
+      return "unsupported dtype (float32, float64, complex64 and complex128 are supported)";
+    case FX_ERR_SHAPE:
+      return "bad shape: batch and n must be >= 0 and n <= 46000";
+    case FX_ERR_PREC:
+      return "prec must be 'tf32x3' or 'ieee'; 'tf32x3' applies to float32 / complex64 only";
+    case FX_ERR_WORKSPACE:
+      return "workspace missing or smaller than one matrix slot (see fermix_workspace_bytes)";
+    case FX_ERR_NULL:
+      return "a required pointer is NULL";
+    case FX_ERR_CUDA:
+      return "CUDA launch or attribute call failed";
+    case FX_ERR_DEVICE:
+      return "no usable CUDA device";
+  }
+  return "unknown error code";
+}
+
+int fermix_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,109 @@
+/* fermix_b200: batched slogdet / slogpf / det / pf on NVIDIA B200 (sm_100a).
+ *
+ * C ABI of libfermix_b200.so. Plain pointers and sizes only. Every entry point is
+ * stream-ordered (no host synchronisation), allocates nothing, and returns 0 or one of
+ * the FX_ERR_* codes; numerical singularity is not an error (it gives sign 0 and
+ * logabs -inf). The caller owns all memory: inputs, outputs and the optional
+ * workspace (size from fermix_workspace_bytes; only matrices too large for one
+ * block's shared memory use it).
+ *
+ * Arrays are C-contiguous: a (batch, n, n) row-major, complex values interleaved
+ * (re, im) as in numpy / torch / XLA; sign, value and coef have the input dtype,
+ * logabs the real dtype.
+ *
+ * Reference interfaces these entry points replace (ChenAo-Phys/fermix, paths relative
+ * to that project; the reference reaches its kernels through pl.pallas_call, wrapped by
+ * _pcall in src/fermix/_field.py:357-389):
+ *   fermix_slogdet       <- _slogdet_core / _lu_core       src/fermix/_diff.py:42-49, src/fermix/_lu.py:543-611
+ *   fermix_slogdet_grad  <- _parts / _lu_parts, _det_gradT src/fermix/_diff.py:62-77, src/fermix/_inverse.py:502-531,
+ *                                                          src/fermix/_diff.py:205-246
+ *   fermix_slogpf        <- _slogpf_core / _pf_core        src/fermix/_diff.py:52-59, src/fermix/_pf.py:497-502
+ *   fermix_slogpf_grad   <- _pf_grad_parts / _pf_parts     src/fermix/_diff.py:80-89, src/fermix/_pfinv.py:196-269
+ *   fermix_workspace_bytes, fermix_strerror, fermix_check_prec
+ *                        <- Field.check_prec / PREC        src/fermix/_field.py:20-23, :262-275
+ */
+#ifndef FERMIX_B200_H
+#define FERMIX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes (src/fermix/_field.py:24-29, KINDS) */
+#define FX_F32 0
+#define FX_F64 1
+#define FX_C64 2
+#define FX_C128 3
+
+/* prec codes (src/fermix/_field.py:20-23, PREC): 0 = the dtype's default
+ * ("tf32x3" for float32 / complex64, "ieee" otherwise) */
+#define FX_PREC_DEFAULT 0
+#define FX_PREC_TF32X3 1
+#define FX_PREC_IEEE 2
+
+/* ops for fermix_workspace_bytes */
+#define FX_OP_SLOGDET 0
+#define FX_OP_SLOGPF 1
+
+/* error codes */
+#define FX_OK 0
+#define FX_ERR_DTYPE 1     /* unsupported dtype code */
+#define FX_ERR_SHAPE 2     /* batch < 0 or n < 0 (or n too large for int indexing) */
+#define FX_ERR_PREC 3      /* prec unknown, or tf32x3 with a 64-bit dtype */
+#define FX_ERR_WORKSPACE 4 /* workspace missing or smaller than one matrix slot */
+#define FX_ERR_NULL 5      /* a required pointer is NULL */
+#define FX_ERR_CUDA 6      /* a CUDA launch / attribute call failed */
+#define FX_ERR_DEVICE 7    /* no usable CUDA device */
+
+/* (sign, logabs) of each matrix; value = sign * exp(logabs) (det) or, for n <= 4, the
+ * explicit polynomial. value may be NULL. Replaces _slogdet_core / _lu_core. */
+int fermix_slogdet(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a, void* sign,
+                   void* logabs, void* value, void* workspace, size_t workspace_bytes);
+
+/* The forward plus the gradient matrix of each member, scaled by coef[b] (NULL = 1) and
+ * conjugated when conj_out != 0:
+ *   adjugate == 0: grad = coef * A^-T (slogdet; zero for an exactly singular or
+ *                  non-finite member)            -- _lu_parts, src/fermix/_inverse.py:502-531
+ *   adjugate != 0: grad = coef * adj(A)^T (det; finite for singular A, exact for up to two
+ *                  zero pivots)                  -- _det_gradT, src/fermix/_diff.py:205-246
+ * (sign, logabs, value) are bit-identical to fermix_slogdet on the same input. */
+int fermix_slogdet_grad(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a,
+                        const void* coef, int conj_out, int adjugate, void* sign, void* logabs, void* value,
+                        void* grad, void* workspace, size_t workspace_bytes);
+
+/* (sign, logabs) of the Pfaffian of S = (a - a^T) / 2 (skew_symmetrize != 0) or of the
+ * skew input a itself; odd n gives (0, -inf). Replaces _slogpf_core / _pf_core. */
+int fermix_slogpf(void* stream, int dtype, int prec, int64_t batch, int64_t n, int skew_symmetrize, const void* a,
+                  void* sign, void* logabs, void* value, void* workspace, size_t workspace_bytes);
+
+/* The forward plus the gradient w.r.t. a of each member, scaled by coef[b]:
+ *   adjugate == 0: grad = coef * S^-T / 2 = -coef * S^-1 / 2 (slogpf; zero for an exactly
+ *                  singular member)              -- _pf_parts(adjugate=False)
+ *   adjugate != 0: grad = coef * pf(S) S^-T / 2 (pf; the Pfaffian adjugate, finite for
+ *                  singular S)                   -- _pf_parts(adjugate=True), src/fermix/_pfinv.py:196-269
+ * Odd n gives a zero gradient. (sign, logabs, value) equal fermix_slogpf bit for bit. */
+int fermix_slogpf_grad(void* stream, int dtype, int prec, int64_t batch, int64_t n, int skew_symmetrize,
+                       const void* a, const void* coef, int conj_out, int adjugate, void* sign, void* logabs,
+                       void* value, void* grad, void* workspace, size_t workspace_bytes);
+
+/* Workspace bytes a call needs on the current device (0 when every matrix fits in one
+ * block's shared memory); grad != 0 for the *_grad entry points. */
+size_t fermix_workspace_bytes(int op, int dtype, int64_t batch, int64_t n, int grad);
+
+/* FX_OK when prec is valid for dtype (Field.check_prec, src/fermix/_field.py:265-275). */
+int fermix_check_prec(int dtype, int prec);
+
+/* Static description of an error code. */
+const char* fermix_strerror(int code);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int fermix_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FERMIX_B200_H */
