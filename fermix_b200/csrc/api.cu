@@ -15,6 +15,7 @@
 #include "fermix_b200.h"
 #include "fused_pf.cuh"
 #include "poly.cuh"
+#include "small.cuh"
 
 namespace {
 
@@ -53,35 +54,59 @@ int validate(int dtype, int prec, int64_t batch, int64_t n) {
 int threads_for(int n) { return n <= 24 ? 32 : (n <= 64 ? 128 : 256); }
 
 // Launch geometry of one fused call (shared by the launch and the workspace query).
-template <typename T>
 struct Plan {
   int threads = 0, ld = 0, in_smem = 0;
   size_t smem = 0, slot = 0;
   int64_t grid = 0;
+  void* kernel = nullptr;
 };
 
-template <typename T, bool PF>
-void* fused_kernel_ptr() {
-  return PF ? reinterpret_cast<void*>(&pf_fused_kernel<T>) : reinterpret_cast<void*>(&lu_fused_kernel<T>);
-}
+constexpr int kSmallMax = 256;  // register-panel kernels: ceil(n / 32) <= 8 rows per lane
+
+int rows_per_lane(int n) { return n <= 32 ? 1 : (n <= 64 ? 2 : (n <= 128 ? 4 : 8)); }
 
 template <typename T, bool PF>
-int plan_fused(int64_t batch, int n, int mode, Plan<T>& P) {
+void* small_kernel_ptr(int rs) {
+  switch (rs) {
+    case 1:
+      return PF ? (void*)&pf_small_kernel<T, 1> : (void*)&lu_small_kernel<T, 1>;
+    case 2:
+      return PF ? (void*)&pf_small_kernel<T, 2> : (void*)&lu_small_kernel<T, 2>;
+    case 4:
+      return PF ? (void*)&pf_small_kernel<T, 4> : (void*)&lu_small_kernel<T, 4>;
+    default:
+      return PF ? (void*)&pf_small_kernel<T, 8> : (void*)&lu_small_kernel<T, 8>;
+  }
+}
+
+// Buffers per matrix: pf uses one in-place buffer for forward and gradient; LU needs a
+// second one for the inverse.
+template <typename T, bool PF>
+int plan_fused(int64_t batch, int n, int mode, Plan& P) {
   const DevInfo* D = dev_info();
   if (!D) return FX_ERR_DEVICE;
-  const int nbuf = mode == MODE_FWD ? 1 : 2;
+  const bool small = n <= kSmallMax;
+  const int nbuf = (PF && small) ? 1 : (mode == MODE_FWD ? 1 : 2);
   P.threads = threads_for(n);
   const int ld_s = (n % 2 == 0) ? n + 1 : n;  // odd stride: conflict-free column access
-  const size_t full = SmemLayout<T>::bytes(n, ld_s, nbuf, true);
+  auto bytes = [&](int ld, bool in_smem) -> size_t {
+    if (small) return PF ? Small<T>::bytes(n, ld, in_smem) : LuSmall<T>::bytes(n, ld, nbuf, in_smem);
+    return SmemLayout<T>::bytes(n, ld, nbuf, in_smem);
+  };
+  const size_t full = bytes(ld_s, true);
   P.in_smem = full <= (size_t)D->smem_optin;
   P.ld = P.in_smem ? ld_s : n;
-  P.smem = P.in_smem ? full : SmemLayout<T>::bytes(n, n, nbuf, false);
+  P.smem = P.in_smem ? full : bytes(n, false);
   P.slot = P.in_smem ? 0 : (size_t)nbuf * n * n * sizeof(T);
-  void* k = fused_kernel_ptr<T, PF>();
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem) != cudaSuccess)
+  if (small)
+    P.kernel = small_kernel_ptr<T, PF>(rows_per_lane(n));
+  else
+    P.kernel = PF ? (void*)&pf_fused_kernel<T> : (void*)&lu_fused_kernel<T>;
+  if (cudaFuncSetAttribute(P.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem) != cudaSuccess)
     return FX_ERR_CUDA;
   int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, P.threads, P.smem) != cudaSuccess) return FX_ERR_CUDA;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, P.kernel, P.threads, P.smem) != cudaSuccess)
+    return FX_ERR_CUDA;
   if (occ < 1) occ = 1;
   P.grid = batch < (int64_t)D->sms * occ ? batch : (int64_t)D->sms * occ;
   return FX_OK;
@@ -89,7 +114,7 @@ int plan_fused(int64_t batch, int n, int mode, Plan<T>& P) {
 
 template <typename T, bool PF>
 int launch_fused(cudaStream_t s, Job<T> J, void* ws, size_t ws_bytes) {
-  Plan<T> P;
+  Plan P;
   int e = plan_fused<T, PF>(J.B, J.n, J.mode, P);
   if (e) return e;
   J.ld = P.ld;
@@ -104,11 +129,10 @@ int launch_fused(cudaStream_t s, Job<T> J, void* ws, size_t ws_bytes) {
     J.ws = static_cast<T*>(ws);
   }
   if (grid < 1) return FX_OK;
-  if (PF)
-    pf_fused_kernel<T><<<(unsigned)grid, P.threads, P.smem, s>>>(J);
-  else
-    lu_fused_kernel<T><<<(unsigned)grid, P.threads, P.smem, s>>>(J);
-  return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+  void* args[] = {&J};
+  if (cudaLaunchKernel(P.kernel, dim3((unsigned)grid), dim3(P.threads), args, P.smem, s) != cudaSuccess)
+    return FX_ERR_CUDA;
+  return FX_OK;
 }
 
 template <typename T>
@@ -181,7 +205,7 @@ size_t ws_bytes_t(int op, int64_t batch, int64_t n, int grad) {
   const int mode = grad ? MODE_SLOG_GRAD : MODE_FWD;
   if (op == FX_OP_SLOGDET && n <= DET_POLY_MAX) return 0;
   if (op == FX_OP_SLOGPF && (n % 2 == 1 || n <= PF_POLY_MAX)) return 0;
-  Plan<T> P;
+  Plan P;
   int e = op == FX_OP_SLOGPF ? plan_fused<T, true>(batch, (int)n, mode, P) : plan_fused<T, false>(batch, (int)n, mode, P);
   if (e || P.in_smem) return 0;
   return (size_t)P.grid * P.slot;

@@ -327,35 +327,16 @@ struct SmemLayout {
   }
 };
 
+// Gradient epilogue after the factorisation (A: packed LU in LAPACK order, ipiv the
+// interchanges): X = U~^-1 L^-1 into W, then
+//   slogdet: G = coef * A^-T (zero for singular / non-finite members),
+//   det:     G = coef * adj(A)^T (det * A^-T, or the Woodbury rank-1 form for one or two
+//            exact zero pivots, _diff.py:205-246),
+// and the forward's (sign, logabs, value).
 template <typename T>
-__global__ void __launch_bounds__(256) lu_fused_kernel(Job<T> J) {
+__device__ void lu_gradient_epilogue(const Job<T>& J, int64_t b, T* A, T* W, int ld, int n, const int* ipiv,
+                                     int* sigma, T* vec0, T* vec1, FacState<T>* st) {
   typedef typename Sc<T>::R R;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int n = J.n, ld = J.ld;
-  const int nbuf = J.mode == MODE_FWD ? 1 : 2;
-  T* bufs = J.in_smem ? reinterpret_cast<T*>(smem_raw) : J.ws + (int64_t)blockIdx.x * nbuf * n * ld;
-  unsigned char* tail = smem_raw + (J.in_smem ? (size_t)nbuf * n * ld * sizeof(T) : 0);
-  T* vec0 = reinterpret_cast<T*>(tail);
-  T* vec1 = vec0 + n;
-  FacState<T>* st = reinterpret_cast<FacState<T>*>(vec1 + n);
-  int* ipiv = reinterpret_cast<int*>(st + 1);
-  int* sigma = ipiv + n;
-  T* A = bufs;
-  T* W = bufs + (size_t)n * ld;
-
-  for (int64_t b = blockIdx.x; b < J.B; b += gridDim.x) {
-    load_matrix(J, b, A, ld, false);
-    __syncthreads();
-    lu_factor(A, ld, n, ipiv, st);
-    if (J.mode == MODE_FWD) {
-      if (threadIdx.x == 0) {
-        J.sign[b] = st->sign;
-        J.logabs[b] = st->logabs;
-        if (J.value) J.value[b] = scale(st->sign, rexp(st->logabs));
-      }
-      __syncthreads();
-      continue;
-    }
     // ---- gradient: X = U~^-1 L^-1, then A^-T[i][j] = X[j][sigma(i)]
     if (threadIdx.x == 0) {
       for (int j = 0; j < n; ++j) sigma[j] = j;
@@ -439,6 +420,38 @@ __global__ void __launch_bounds__(256) lu_fused_kernel(Job<T> J) {
       if (J.value) J.value[b] = scale(s.sign, rexp(s.logabs));
     }
     __syncthreads();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) lu_fused_kernel(Job<T> J) {
+  typedef typename Sc<T>::R R;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int n = J.n, ld = J.ld;
+  const int nbuf = J.mode == MODE_FWD ? 1 : 2;
+  T* bufs = J.in_smem ? reinterpret_cast<T*>(smem_raw) : J.ws + (int64_t)blockIdx.x * nbuf * n * ld;
+  unsigned char* tail = smem_raw + (J.in_smem ? (size_t)nbuf * n * ld * sizeof(T) : 0);
+  T* vec0 = reinterpret_cast<T*>(tail);
+  T* vec1 = vec0 + n;
+  FacState<T>* st = reinterpret_cast<FacState<T>*>(vec1 + n);
+  int* ipiv = reinterpret_cast<int*>(st + 1);
+  int* sigma = ipiv + n;
+  T* A = bufs;
+  T* W = bufs + (size_t)n * ld;
+
+  for (int64_t b = blockIdx.x; b < J.B; b += gridDim.x) {
+    load_matrix(J, b, A, ld, false);
+    __syncthreads();
+    lu_factor(A, ld, n, ipiv, st);
+    if (J.mode == MODE_FWD) {
+      if (threadIdx.x == 0) {
+        J.sign[b] = st->sign;
+        J.logabs[b] = st->logabs;
+        if (J.value) J.value[b] = scale(st->sign, rexp(st->logabs));
+      }
+      __syncthreads();
+      continue;
+    }
+    lu_gradient_epilogue(J, b, A, W, ld, n, ipiv, sigma, vec0, vec1, st);
   }
 }
 

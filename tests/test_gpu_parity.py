@@ -395,3 +395,31 @@ def test_n300_forward_and_grad(dtype):
     assert np.array_equal(s, s2) and np.array_equal(l, l2)
     inv = np.linalg.inv(ref64(A))
     assert relerr(g, np.swapaxes(inv, -1, -2)) < tol(dtype, 1e-3, 1e-9)
+
+
+@pytest.mark.parametrize(
+    "dtype,n",
+    [(np.float32, 236), (np.float32, 240), (np.float64, 170), (np.complex64, 170), (np.complex128, 120)],
+    ids=["f32-236-smem", "f32-240-ws", "f64-170-ws", "c64-170-ws", "c128-120-ws"],
+)
+def test_register_panel_shared_and_workspace_modes(dtype, n):
+    """The register-panel kernels (n <= 256) with the matrix in shared memory and, once
+    it no longer fits, in the global workspace: forward, primal under the gradient, and
+    both gradients against the 64-bit references."""
+    gen = np.random.default_rng(40 + n)
+    A = randn((2, n, n), dtype, gen)
+    s, l = slogdet(A)
+    s64, l64 = np.linalg.slogdet(ref64(A))
+    assert_sign(s, s64, dtype, log_tol(dtype, n))
+    assert np.max(np.abs(l - l64)) < log_tol(dtype, n)
+    s2, l2, g = host(fx.slogdet_parts(cuda(A)))
+    assert np.array_equal(s, s2) and np.array_equal(l, l2)
+    assert relerr(g, np.swapaxes(np.linalg.inv(ref64(A)), -1, -2)) < tol(dtype, 3e-3, 1e-9)
+    S = skew(randn((2, n, n), dtype, gen))
+    s, l = slogpf(S, skew_symmetrize=False)
+    ref = [pf_ref64(S[i]) for i in range(2)]
+    assert_sign(s, [r[0] for r in ref], dtype, log_tol(dtype, n))
+    assert np.max(np.abs(l - [r[1] for r in ref])) < log_tol(dtype, n)
+    s2, l2, g = host(fx.slogpf_parts(cuda(S), skew_symmetrize=False))
+    assert np.array_equal(s, s2) and np.array_equal(l, l2)
+    assert relerr(g, 0.5 * np.swapaxes(np.linalg.inv(ref64(S)), -1, -2)) < tol(dtype, 3e-3, 1e-9)
