@@ -104,6 +104,9 @@ int plan_fused(int64_t batch, int n, int mode, Plan& P) {
     P.kernel = PF ? (void*)&pf_fused_kernel<T> : (void*)&lu_fused_kernel<T>;
   if (cudaFuncSetAttribute(P.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem) != cudaSuccess)
     return FX_ERR_CUDA;
+  // shared memory over L1: these kernels keep their matrices in shared memory
+  if (cudaFuncSetAttribute(P.kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    return FX_ERR_CUDA;
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, P.kernel, P.threads, P.smem) != cudaSuccess)
     return FX_ERR_CUDA;
@@ -313,5 +316,17 @@ const char* fermix_strerror(int code) {
 }
 
 int fermix_version(void) { return 100; }
+
+#ifdef FX_PHASE_TIMERS
+// profiling builds only: copy out / reset the per-phase cycle counters
+int fermix_debug_phase_cycles(unsigned long long* out, int reset) {
+  if (cudaMemcpyFromSymbol(out, fx::fx_phase_cycles, sizeof(unsigned long long) * 16) != cudaSuccess) return 1;
+  if (reset) {
+    unsigned long long z[16] = {0};
+    if (cudaMemcpyToSymbol(fx::fx_phase_cycles, z, sizeof(z)) != cudaSuccess) return 1;
+  }
+  return 0;
+}
+#endif
 
 }  // extern "C"

@@ -284,4 +284,19 @@ struct KSum {
   }
 };
 
+// Optional per-phase cycle counters for profiling builds (-DFX_PHASE_TIMERS): thread 0
+// of each block adds clock64() deltas into fx_phase_cycles[phase].
+#ifdef FX_PHASE_TIMERS
+__device__ unsigned long long fx_phase_cycles[16];
+#define FX_TIC(var) long long var = clock64()
+#define FX_TOC(var, ph)                                                              \
+  do {                                                                               \
+    if (threadIdx.x == 0) atomicAdd(&fx_phase_cycles[ph], (unsigned long long)(clock64() - var)); \
+    var = clock64();                                                                 \
+  } while (0)
+#else
+#define FX_TIC(var)
+#define FX_TOC(var, ph)
+#endif
+
 }  // namespace fx

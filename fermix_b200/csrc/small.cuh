@@ -37,6 +37,54 @@ __device__ __forceinline__ int first_unassigned(uint32_t unas, int lane) {
   return (int)__reduce_min_sync(0xffffffffu, cand);
 }
 
+
+// (sign, logabs, nzero) of prod_k d_k (k < cnt, d_k = piv(k)), reduced by warp 0 in a
+// fixed order (lanes stride the pivots, then a butterfly), so every kernel that calls it
+// on the same pivots returns the same bits. Real signs are products of +-1 (exact).
+template <typename T, typename F>
+__device__ void warp_sign_log(int cnt, F piv, int parity, PfState<T>* out_pf, FacState<T>* out_lu) {
+  typedef typename Sc<T>::R R;
+  const int lane = threadIdx.x & 31;
+  if ((threadIdx.x >> 5) != 0) return;
+  T sg = s_one<T>();
+  KSum<R> ls;
+  ls.init();
+  int nz = 0;
+  for (int k = lane; k < cnt; k += 32) {
+    const T d = piv(k);
+    sg = mul(sg, unit(d));
+    ls.add(rlog(mag(d)));
+    nz += is_zero(d);
+  }
+  R lsum = ls.value();
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const T o = shfl_idx(sg, lane ^ off);
+    sg = mul(sg, o);
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+    nz += __shfl_xor_sync(0xffffffffu, nz, off);
+  }
+  if (lane == 0) {
+    if (parity) sg = neg(sg);
+    if (nz) sg = s_zero<T>();
+    if constexpr (Sc<T>::cx) {
+      R m = rhypot(sg.re, sg.im);
+      if (m != R(0)) sg = {rdiv(sg.re, m), rdiv(sg.im, m)};
+    }
+    const R la = nz ? R(-INFINITY) : lsum;
+    if (out_pf) {
+      out_pf->sign = sg;
+      out_pf->logabs = la;
+      out_pf->nzero = nz;
+    }
+    if (out_lu) {
+      out_lu->sign = sg;
+      out_lu->logabs = la;
+      out_lu->nzero = nz;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ Parlett-Reid
 template <typename T, int RS>
 struct PfNP {
@@ -54,11 +102,9 @@ __device__ void pf2_factor(T* M, int ld, int n, int* perm, int* at, int* pof, in
   typedef typename Sc<T>::R R;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < n; i += nthr()) perm[i] = i;
-  T sgn = s_one<T>();
-  KSum<R> ls;
-  ls.init();
-  int par = 0, nzero = 0;
+  int par = 0;
   __syncthreads();
+  FX_TIC(tp0);
   for (int k0 = 0; k0 < n; k0 += 2 * NP) {
     const int np = min(NP, (n - k0) / 2);
     if (warp == 0) {
@@ -155,39 +201,30 @@ __device__ void pf2_factor(T* M, int ld, int n, int* perm, int* at, int* pof, in
           if (lane == 0) {
             const int q = pof[p];
             ipiv[c + 1] = q;
+            dvec[c >> 1] = d;
             if (q != c + 1) {
               const int x = at[c + 1];
               at[c + 1] = p;
               at[q] = x;
               pof[p] = c + 1;
               pof[x] = q;
+              const int t = perm[c + 1];
+              perm[c + 1] = perm[q];
+              perm[q] = t;
               par ^= 1;
             }
-            dvec[c >> 1] = d;
-            sgn = mul(sgn, unit(d));
-            ls.add(rlog(mag(d)));
-            nzero += is_zero(d);
           }
           __syncwarp();
         }
       }
     }
     __syncthreads();
+    FX_TOC(tp0, 0);
     // the panel's interchanges, rows (all columns) then columns (rows >= k0)
     for (int x = tid; x < n; x += nthr()) {
       for (int s = 0; s < np; ++s) {
         const int c1 = k0 + 2 * s + 1, q = ipiv[c1];
         if (q != c1) swap_(M[c1 * ld + x], M[q * ld + x]);
-      }
-    }
-    if (tid == 0) {
-      for (int s = 0; s < np; ++s) {
-        const int c1 = k0 + 2 * s + 1, q = ipiv[c1];
-        if (q != c1) {
-          const int t = perm[c1];
-          perm[c1] = perm[q];
-          perm[q] = t;
-        }
       }
     }
     __syncthreads();
@@ -198,20 +235,15 @@ __device__ void pf2_factor(T* M, int ld, int n, int* perm, int* at, int* pof, in
       }
     }
     __syncthreads();
+    FX_TOC(tp0, 1);
     pf_trailing<T, TileShape<T>::MI, TileShape<T>::MJ>(M, ld, k0 + 2 * np, n, k0, np);
     __syncthreads();
+    FX_TOC(tp0, 2);
   }
+  warp_sign_log<T>(n / 2, [&](int k) { return dvec[k]; }, par, st, (FacState<T>*)nullptr);
+  __syncwarp();
   if (tid == 0) {
-    if (par) sgn = neg(sgn);
-    if (nzero) sgn = s_zero<T>();
-    if constexpr (Sc<T>::cx) {
-      R m = rhypot(sgn.re, sgn.im);
-      if (m != R(0)) sgn = {rdiv(sgn.re, m), rdiv(sgn.im, m)};
-    }
-    st->sign = sgn;
-    st->logabs = nzero ? -INFINITY : ls.value();
     st->parity = par;
-    st->nzero = nzero;
     const int h = n / 2;
     int K = 0;
     R bm = R(INFINITY);
@@ -315,13 +347,16 @@ __device__ void pf2_evaluate(T* M, int ld, int n, const T* dvec, int lift_s, T l
   }
   for (int i = threadIdx.x; i < n; i += nthr()) pos[perm[i]] = i;
   __syncthreads();
+  FX_TIC(te0);
   // L~: column 2s (w_s) scaled by 1 / d~_s
   for (int idx = threadIdx.x; idx < h * n; idx += nthr()) {
     const int s = idx / n, i = idx - s * n;
     if (i > 2 * s + 1) M[i * ld + 2 * s] = mul(M[i * ld + 2 * s], dinv[s]);
   }
   __syncthreads();
+  FX_TOC(te0, 3);
   tri_inv_unit_lower_inplace(M, ld, n);
+  FX_TOC(te0, 4);
   // R = Y^T D~^-1 Y, lower triangle R[i][j] (i > j) stored at M[j][i]
   {
     const int TC = 16, MI = TileShape<T>::MI, MJ = TileShape<T>::MJ;
@@ -381,6 +416,7 @@ __device__ void pf2_evaluate(T* M, int ld, int n, const T* dvec, int lift_s, T l
     if (bad) st->bad = 1;
   }
   __syncthreads();
+  FX_TOC(te0, 5);
   const int aK = 2 * K;
   // w[i] = R[i][aK], v[i] = Y[aK][i] (position order)
   T* wvec = wv;
@@ -425,6 +461,7 @@ __device__ void pf2_evaluate(T* M, int ld, int n, const T* dvec, int lift_s, T l
     out[idx] = v;
   }
   __syncthreads();
+  FX_TOC(te0, 6);
 }
 
 template <typename T>
@@ -514,10 +551,7 @@ template <typename T, int RS, int NB>
 __device__ void lu2_factor(T* M, int ld, int n, int* ipiv, int* at, int* pof, FacState<T>* st) {
   typedef typename Sc<T>::R R;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  T sgn = s_one<T>();
-  KSum<R> ls;
-  ls.init();
-  int par = 0, nzero = 0, k1z = -1, k2z = -1;
+  int par = 0, k1z = -1, k2z = -1;
   for (int k0 = 0; k0 < n; k0 += NB) {
     const int kb = min(NB, n - k0);
     if (warp == 0) {
@@ -589,12 +623,9 @@ __device__ void lu2_factor(T* M, int ld, int n, int* ipiv, int* at, int* pof, Fa
               pof[x] = q;
               par ^= 1;
             }
-            sgn = mul(sgn, unit(piv));
-            ls.add(rlog(mag(piv)));
             if (z) {
               if (k1z < 0) k1z = j;
               k2z = j;
-              ++nzero;
             }
           }
           __syncwarp();
@@ -633,17 +664,11 @@ __device__ void lu2_factor(T* M, int ld, int n, int* ipiv, int* at, int* pof, Fa
     lu_trailing<T, TileShape<T>::MI, TileShape<T>::MJ>(M, ld, k0 + kb, n, k0, kb);
     __syncthreads();
   }
+  // the pivots are U's diagonal
+  warp_sign_log<T>(n, [&](int k) { return M[k * ld + k]; }, par, (PfState<T>*)nullptr, st);
+  __syncwarp();
   if (tid == 0) {
-    if (par) sgn = neg(sgn);
-    if (nzero) sgn = s_zero<T>();
-    if constexpr (Sc<T>::cx) {
-      R m = rhypot(sgn.re, sgn.im);
-      if (m != R(0)) sgn = {rdiv(sgn.re, m), rdiv(sgn.im, m)};
-    }
-    st->sign = sgn;
-    st->logabs = nzero ? -INFINITY : ls.value();
     st->parity = par;
-    st->nzero = nzero;
     st->k1 = k1z;
     st->k2 = k2z;
     st->bad = 0;
