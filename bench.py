@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the batched slogpf / slogdet path on 1..8 B200s.
 
-Default workload: slogpf forward + VJP of logabs, float32,
+Default workload (the headline configuration): slogpf forward + VJP of logabs, float32,
 batch 4096 of skew-symmetric S = A - A^T, A 128x128 iid N(0,1), prec="tf32x3". One step
 is one pass over the batch: sign, logabs and the gradient S^-T/2 of sum(logabs) from one
 fused launch through the C ABI (fermix_slogpf_grad). Scaling is weak: each rank
