@@ -29,6 +29,13 @@ sys.path.insert(0, ROOT)
 
 METRIC = "slogdet/slogpf matrices/sec fwd & fwd+bwd at 1-8 B200; % of roofline"
 KERNEL = {"slogpf": "pf_fused_kernel", "slogdet": "lu_fused_kernel"}
+SMALL_KERNEL = {"slogpf": "pf_small_kernel", "slogdet": "lu_small_kernel"}
+
+
+def kernel_name(a):
+    """The kernel the library dispatches this workload to (register-panel kernels up to
+    n = 256, the one-block-per-matrix generic kernels above)."""
+    return (SMALL_KERNEL if a.n <= 256 else KERNEL)[a.op]
 
 
 def parse():
@@ -80,7 +87,7 @@ def peaks():
 def traffic_from_profiles(a):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary
     (a line 'traffic_bytes_per_launch: X' for this workload), else None."""
-    name = f"{KERNEL[a.op]}_{a.dtype}_n{a.n}_{'fwd' if a.fwd_only else 'fwdbwd'}.md"
+    name = f"{kernel_name(a)}_{a.dtype}_n{a.n}_{'fwd' if a.fwd_only else 'fwdbwd'}.md"
     p = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(p):
         return None
@@ -168,7 +175,7 @@ def cpu_rate(a, count, threads):
             if a.fwd_only:
                 F.slogpf(S)
             else:
-                F.slogpf(S), F.slogpf_grad(S)
+                F.pf_parts(S, False)  # one factor-keeping Parlett-Reid: (sign, logabs, S^-1)
         else:
             if a.fwd_only:
                 F.slogdet(A)
@@ -324,7 +331,7 @@ def main():
         "frac": achieved / hbm,
         "traffic": traffic_from_profiles(a),
         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-        "kernel": KERNEL[a.op],
+        "kernel": kernel_name(a),
         "algorithmic_bytes_per_launch": B * by,
         "flops_per_launch": B * fl,
         "achieved_tflops": B * fl / launch_s / 1e12,

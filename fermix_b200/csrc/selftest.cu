@@ -1,0 +1,90 @@
+// Self-test of the tensor-core building blocks (umma.cuh) on the running GPU: one
+// 128 x 128 x 16 update D = C +- A B^T in TMEM with the 3xTF32 split, read back to
+// global memory. Used by the GPU tests to pin the descriptor and TMEM conventions
+// before the TMEM-resident kernels rely on them.
+#include <cuda_runtime.h>
+
+#include "fermix_b200.h"
+#include "umma.cuh"
+
+namespace {
+
+using namespace fx::umma;
+
+constexpr int kM = 128, kN = 128, kK = 16;
+constexpr uint32_t kSlab = kM * 8 * 4;  // bytes of one K = 8 slab of a 128-row operand
+
+__global__ void __launch_bounds__(128) umma_selftest_kernel(const float* A, const float* B, const float* C, float* D,
+                                                            int negate, int* status) {
+  __shared__ __align__(1024) float sAhi[kM * kK], sAlo[kM * kK], sBhi[kN * kK], sBlo[kN * kK];
+  __shared__ uint32_t tslot;
+  __shared__ __align__(8) uint64_t mbar;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (warp == 0) {
+    tmem_alloc(&tslot, 128);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&mbar, 1);
+    fence_mbar_init();
+  }
+  // operands, split into TF32 hi / lo parts, in the K-major interleaved layout
+  {
+    const int r = tid;
+    for (int k = 0; k < kK; ++k) {
+      const uint32_t off = kmajor_offset(r, k, kSlab) / 4;
+      float a = A[r * kK + k], ah = tf32_round(a);
+      sAhi[off] = ah;
+      sAlo[off] = tf32_round(a - ah);
+      float b = B[r * kK + k], bh = tf32_round(b);
+      sBhi[off] = bh;
+      sBlo[off] = tf32_round(b - bh);
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tbase = tslot;
+  const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);
+  for (int c = 0; c < kN; ++c) tmem_st1(trow + c, __float_as_uint(C[tid * kN + c]));
+  tmem_wait_st();
+  fence_proxy_async_smem();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  if (tid == 0) {
+    const uint32_t idesc = idesc_tf32(kM, kN, negate != 0);
+    for (int s = 0; s < kK / 8; ++s) {
+      const uint64_t ahi = smem_desc_kmajor(smem_u32(sAhi) + s * kSlab, 128, 256);
+      const uint64_t alo = smem_desc_kmajor(smem_u32(sAlo) + s * kSlab, 128, 256);
+      const uint64_t bhi = smem_desc_kmajor(smem_u32(sBhi) + s * kSlab, 128, 256);
+      const uint64_t blo = smem_desc_kmajor(smem_u32(sBlo) + s * kSlab, 128, 256);
+      mma_tf32(tbase, ahi, bhi, idesc, true);
+      mma_tf32(tbase, ahi, blo, idesc, true);
+      mma_tf32(tbase, alo, bhi, idesc, true);
+    }
+    mma_commit(&mbar);
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(&mbar, 0, 1u << 24);
+  fence_after_sync();
+  for (int c = 0; c < kN; c += 8) {
+    uint32_t v[8];
+    tmem_ld8(trow + c, v);
+    tmem_wait_ld();
+    for (int j = 0; j < 8; ++j) D[tid * kN + c + j] = __uint_as_float(v[j]);
+  }
+  if (!ok) atomicOr(status, 1);
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 128);
+}
+
+}  // namespace
+
+extern "C" int fermix_selftest_umma(void* stream, const float* a, const float* b, const float* c, float* d, int negate,
+                                    int* status) {
+  if (!a || !b || !c || !d || !status) return FX_ERR_NULL;
+  umma_selftest_kernel<<<1, 128, 0, static_cast<cudaStream_t>(stream)>>>(a, b, c, d, negate, status);
+  return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+}
