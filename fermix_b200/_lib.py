@@ -27,7 +27,7 @@ SIGNATURES = {
     "fermix_check_prec": (_i, [_i, _i]),
     "fermix_strerror": (ctypes.c_char_p, [_i]),
     "fermix_version": (_i, []),
-    "fermix_selftest_umma": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp]),
+    "fermix_selftest_umma": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp]),
 }
 
 _lib = None

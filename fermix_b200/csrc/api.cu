@@ -11,11 +11,13 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "fermix_b200.h"
 #include "fused_pf.cuh"
 #include "poly.cuh"
 #include "small.cuh"
+#include "pf_tc.cuh"
 
 namespace {
 
@@ -115,6 +117,34 @@ int plan_fused(int64_t batch, int n, int mode, Plan& P) {
   return FX_OK;
 }
 
+// Tensor-core slogpf (float32, prec tf32x3, 8 <= n <= 128, forward or slogpf gradient):
+// one 128-thread block per matrix, the matrix resident in TMEM (128 of the SM's 512
+// columns). The shared-memory request is padded so that exactly four blocks share an SM
+// (four blocks use all 512 TMEM columns; a fifth would wait in tcgen05.alloc).
+constexpr size_t kTcSmem = 50 * 1024;
+static_assert(sizeof(PfTcSmem) <= kTcSmem, "PfTcSmem too large");
+
+bool use_pf_tc(int dtype_is_f32, int prec, int n, int mode) {
+  return dtype_is_f32 && prec != FX_PREC_IEEE && n >= 8 && n <= kTcN && (mode == MODE_FWD || mode == MODE_SLOG_GRAD);
+}
+
+int launch_pf_tc(cudaStream_t s, Job<float> J) {
+  const DevInfo* D = dev_info();
+  if (!D) return FX_ERR_DEVICE;
+  void* k = J.mode == MODE_FWD ? (void*)&pf_tc_kernel<false> : (void*)&pf_tc_kernel<true>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem) != cudaSuccess)
+    return FX_ERR_CUDA;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    return FX_ERR_CUDA;
+  // four 128-thread blocks per SM: 4 x 51 KB shared memory, 4 x 128 TMEM columns
+  const int64_t cap = (int64_t)D->sms * 4;
+  const int64_t grid = J.B < cap ? J.B : cap;
+  if (grid < 1) return FX_OK;
+  void* args[] = {&J};
+  if (cudaLaunchKernel(k, dim3((unsigned)grid), dim3(128), args, kTcSmem, s) != cudaSuccess) return FX_ERR_CUDA;
+  return FX_OK;
+}
+
 template <typename T, bool PF>
 int launch_fused(cudaStream_t s, Job<T> J, void* ws, size_t ws_bytes) {
   Plan P;
@@ -173,7 +203,7 @@ int run_det(cudaStream_t s, int64_t batch, int64_t n, const void* a, const void*
 }
 
 template <typename T>
-int run_pf(cudaStream_t s, int64_t batch, int64_t n, int skew, const void* a, const void* coef, int conj_out,
+int run_pf(cudaStream_t s, int prec, int64_t batch, int64_t n, int skew, const void* a, const void* coef, int conj_out,
            int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb) {
   Job<T> J = make_job<T>(batch, n, a, coef, conj_out, skew, mode, sign, logabs, value, grad);
   if (n % 2 == 1) {
@@ -185,6 +215,20 @@ int run_pf(cudaStream_t s, int64_t batch, int64_t n, int skew, const void* a, co
     return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
   }
   if (n <= PF_POLY_MAX) return launch_poly<T>(s, J, 1);
+  if constexpr (std::is_same<T, float>::value) {
+    if (use_pf_tc(1, prec, (int)n, mode)) return launch_pf_tc(s, J);
+    if (mode == MODE_VALUE_GRAD && use_pf_tc(1, prec, (int)n, MODE_FWD)) {
+      // the Pfaffian adjugate comes from the register-panel kernel; the primal it returns
+      // must be the forward's own bits, so the tensor-core forward rewrites
+      // (sign, logabs, value) after it (same stream)
+      int e = launch_fused<T, true>(s, J, ws, wsb);
+      if (e) return e;
+      Job<T> F = J;
+      F.mode = MODE_FWD;
+      F.g = nullptr;
+      return launch_pf_tc(s, F);
+    }
+  }
   return launch_fused<T, true>(s, J, ws, wsb);
 }
 
@@ -208,6 +252,7 @@ size_t ws_bytes_t(int op, int64_t batch, int64_t n, int grad) {
   const int mode = grad ? MODE_SLOG_GRAD : MODE_FWD;
   if (op == FX_OP_SLOGDET && n <= DET_POLY_MAX) return 0;
   if (op == FX_OP_SLOGPF && (n % 2 == 1 || n <= PF_POLY_MAX)) return 0;
+  if (op == FX_OP_SLOGPF && std::is_same<T, float>::value && n <= kTcN) return 0;  // TMEM / shared memory only
   Plan P;
   int e = op == FX_OP_SLOGPF ? plan_fused<T, true>(batch, (int)n, mode, P) : plan_fused<T, false>(batch, (int)n, mode, P);
   if (e || P.in_smem) return 0;
@@ -262,8 +307,8 @@ int fermix_slogpf(void* stream, int dtype, int prec, int64_t batch, int64_t n, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
-    return run_pf<T>(s, batch, n, skew_symmetrize, a, nullptr, 0, MODE_FWD, sign, logabs, value, nullptr, workspace,
-                     workspace_bytes);
+    return run_pf<T>(s, prec, batch, n, skew_symmetrize, a, nullptr, 0, MODE_FWD, sign, logabs, value, nullptr,
+                     workspace, workspace_bytes);
   });
 }
 
@@ -278,8 +323,8 @@ int fermix_slogpf_grad(void* stream, int dtype, int prec, int64_t batch, int64_t
   const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
-    return run_pf<T>(s, batch, n, skew_symmetrize, a, coef, conj_out, mode, sign, logabs, value, grad, workspace,
-                     workspace_bytes);
+    return run_pf<T>(s, prec, batch, n, skew_symmetrize, a, coef, conj_out, mode, sign, logabs, value, grad,
+                     workspace, workspace_bytes);
   });
 }
 

@@ -1,0 +1,478 @@
+// Tensor-memory resident Parlett-Reid "sweep" for float32 slogpf, 8 <= n <= 128,
+// prec = "tf32x3": forward (sign, logabs) and, in the same pass, S^-1 for the gradient.
+//
+// Reference behaviour: the pair steps and pivoting of src/fermix/_fallback.py:266-300
+// (pivot = largest corrected entry of column a among the unassigned rows, d = S[a, p]),
+// blocked as in src/fermix/_pf.py:516-570, with the tf32x3 block updates of
+// src/fermix/_field.py:173-190 (3 TF32 products per update); the gradient is S^-T / 2 of
+// src/fermix/_diff.py:139-154, zero for an exactly singular S (_pfinv.py:263-268).
+//
+// Design (B200). The 128 x 128 matrix lives in tensor memory (TMEM lane i = row i, one
+// 32-bit column per matrix column) for the whole call; thread i of the 128-thread block
+// owns row i. Each panel of up to 8 pairs is found by the pair steps on corrected
+// columns (one TMEM column read per step and thread), then the whole matrix gets the
+// rank-16 block-sweep update D -= W B^T as six tcgen05.mma kind::tf32 instructions
+// (K = 16, hi / lo split) issued by one thread, accumulating in TMEM. In gradient mode the
+// panel's pivot rows and columns are then replaced by the block-sweep values
+//   A'_XP = A_XP A_PP^-1,  A'_PX = -+A'_XP^T,  A'_PP = -A_PP^-1,
+// so that after the last panel TMEM holds -S^-1 (sweeping every index inverts the
+// matrix); the forward-only mode skips the replacement and its (sign, logabs) are
+// bit-identical (the unswept part evolves identically). Row-derived operand values come
+// from the column values by the sweep's sign pattern: skew inside the unswept and inside
+// the swept index sets, symmetric across them.
+#pragma once
+#include "fused_lu.cuh"
+#include "umma.cuh"
+
+namespace fx {
+
+constexpr int kTcN = 128;                        // TMEM lanes / columns of the matrix
+constexpr uint32_t kTcSlab = kTcN * 8 * 4;       // bytes of one K = 8 operand slab
+constexpr uint32_t kTcWaitIters = 1u << 26;       // bounded MMA completion wait
+
+struct PfTcSmem {
+  float u[8][kTcN];  // u_t[x] = col_p[x] / d_t of the panel's pairs (broadcast reads)
+  float v[8][kTcN];  // v_t[x] = -col_a[x] / d_t
+  float whi[kTcN * 16], wlo[kTcN * 16];  // MMA A operand (K-major, interleaved), TF32 hi / lo
+  float bhi[kTcN * 16], blo[kTcN * 16];  // MMA B operand
+  float app[16][17];                     // A_PP of the panel, then A_PP^-1
+  float cand_a[4], cand_c[4];            // per-warp pivot candidates: |value|, value
+  int cand_i[4], cand_f[4];              // index, first live row
+  int at[kTcN], pof[kTcN];               // position -> row, row -> position (virtual pivoting)
+  int pidx[16];                          // the panel's pivot rows a_0, p_0, a_1, p_1, ...
+  unsigned char isP[kTcN];
+  float dvec[kTcN / 2];
+  uint32_t tslot;
+  uint32_t dis[4];  // MMA output-lane mask: lanes that are not pivot rows
+  int parity, bad;
+  uint64_t mbar;
+};
+
+__device__ __forceinline__ void tc_sync() {
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+}
+
+// Inverse of the m x m (m = 2 np <= 16) pivot block in S.app by sequential 2 x 2 pair
+// sweeps (pairs (2q, 2q+1)); warp 0, lane k owns row k. Result: S.app = A_PP^-1.
+__device__ void tc_block_inverse(PfTcSmem& S, int np) {
+  const int lane = threadIdx.x & 31;
+  const int m = 2 * np;
+  float r[16];
+#pragma unroll
+  for (int y = 0; y < 16; ++y) r[y] = (lane < m && y < m) ? S.app[lane][y] : 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    if (q < np) {
+      const int i = 2 * q, j = i + 1;
+      float ri[16], rj[16];
+#pragma unroll
+      for (int y = 0; y < 16; ++y) {
+        ri[y] = __shfl_sync(0xffffffffu, r[y], i);
+        rj[y] = __shfl_sync(0xffffffffu, r[y], j);
+      }
+      const float d00 = ri[i], d01 = ri[j], d10 = rj[i], d11 = rj[j];
+      const float det = d00 * d11 - d01 * d10;
+      const float id = det == 0.f ? 0.f : __fdiv_rn(1.f, det);
+      const float e00 = d11 * id, e01 = -d01 * id, e10 = -d10 * id, e11 = d00 * id;
+      if (lane == i || lane == j) {
+        const float f0 = lane == i ? e00 : e10, f1 = lane == i ? e01 : e11;
+#pragma unroll
+        for (int y = 0; y < 16; ++y)
+          if (y != i && y != j) r[y] = fmaf(f0, ri[y], f1 * rj[y]);
+        r[i] = -f0;
+        r[j] = -f1;
+      } else if (lane < m) {
+        const float xi = r[i], xj = r[j];
+        const float ci = fmaf(xi, e00, xj * e10), cj = fmaf(xi, e01, xj * e11);
+#pragma unroll
+        for (int y = 0; y < 16; ++y)
+          if (y != i && y != j) r[y] = fmaf(-ci, ri[y], fmaf(-cj, rj[y], r[y]));
+        r[i] = ci;
+        r[j] = cj;
+      }
+    }
+  }
+  __syncwarp();
+  if (lane < m) {
+#pragma unroll
+    for (int y = 0; y < 16; ++y)
+      if (y < m) S.app[lane][y] = -r[y];  // the sweep leaves -A_PP^-1
+  }
+}
+
+constexpr int kStageLd = kTcN + 1;  // staged rows: odd stride, conflict-free row reads
+
+// Rows r0 .. r0+31 of the n x n row-major matrix src into stage (stride kStageLd), zero
+// outside n x n; coalesced over the block.
+__device__ __forceinline__ void tc_stage_rows(float* stage, const float* src, int n, int r0) {
+  for (int idx = threadIdx.x; idx < 32 * kTcN; idx += blockDim.x) {
+    const int r = idx >> 7, c = idx & (kTcN - 1);
+    const int row = r0 + r;
+    stage[r * kStageLd + c] = (row < n && c < n) ? __ldg(src + row * n + c) : 0.f;
+  }
+}
+
+template <bool GRAD>
+__global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  PfTcSmem& S = *reinterpret_cast<PfTcSmem*>(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = J.n;
+  const int x = tid;  // this thread's row / TMEM lane
+  if (warp == 0) {
+    umma::tmem_alloc(&S.tslot, kTcN);
+    umma::tmem_relinquish();
+  }
+  if (tid == 0) {
+    umma::mbar_init(&S.mbar, 1);
+    umma::fence_mbar_init();
+  }
+  tc_sync();
+#ifdef FX_PHASE_TIMERS
+  if (blockIdx.x == 0 && tid == 0) fx_phase_cycles[15] = gridDim.x;
+#endif
+  const uint32_t tbase = S.tslot;
+  const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);
+  uint32_t phase = 0;
+
+  for (int64_t b = blockIdx.x; b < J.B; b += gridDim.x) {
+    FX_TIC(tq);
+    // ---- the (skew-symmetrised) matrix into TMEM, zero outside n x n: 32-row chunks
+    // staged through shared memory (coalesced global reads, conflict-free row reads)
+    const float* src = J.a + b * (int64_t)n * n;
+    float* stage = S.whi;  // 32 x kStageLd floats, spans the (idle) operand buffers
+    for (int r0 = 0; r0 < kTcN; r0 += 32) {
+      tc_stage_rows(stage, src, n, r0);
+      __syncthreads();
+      if (warp == (r0 >> 5)) {
+        for (int c0 = 0; c0 < kTcN; c0 += 8) {
+          uint32_t vals[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) vals[j] = __float_as_uint(stage[lane * kStageLd + c0 + j]);
+          umma::tmem_st8(trow + c0, vals);
+        }
+        umma::tmem_wait_st();
+      }
+      __syncthreads();
+    }
+    if (J.skew) {
+      // S = (A - A^T) / 2: the rows of chunk r0 are the columns r0..r0+31 of A^T
+      umma::fence_before_sync();
+      for (int r0 = 0; r0 < kTcN; r0 += 32) {
+        tc_stage_rows(stage, src, n, r0);
+        __syncthreads();
+        umma::fence_after_sync();
+        for (int c0 = r0; c0 < r0 + 32; c0 += 8) {
+          uint32_t vals[8];
+          umma::tmem_ld8(trow + c0, vals);
+          umma::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            vals[j] = __float_as_uint((__uint_as_float(vals[j]) - stage[(c0 + j - r0) * kStageLd + x]) * 0.5f);
+          umma::tmem_st8(trow + c0, vals);
+        }
+        umma::tmem_wait_st();
+        umma::fence_before_sync();
+        __syncthreads();
+      }
+    }
+    S.at[x] = x;
+    S.pof[x] = x;
+    S.isP[x] = 0;
+    if (tid == 0) {
+      S.parity = 0;
+      S.bad = 0;
+    }
+    bool live = x < n;
+    tc_sync();
+    FX_TOC(tq, 8);
+
+    const int npairs = n / 2;
+    for (int g0 = 0; g0 < npairs; g0 += 8) {
+      const int np = min(8, npairs - g0);
+      const bool swept_before = !live && x < n;
+      float ur[8], vr[8], dr[8], s0[16];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        ur[t] = vr[t] = dr[t] = 0.f;
+        s0[2 * t] = s0[2 * t + 1] = 0.f;
+      }
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (s < np) {
+          const int c = 2 * (g0 + s);
+          const int a = S.at[c];
+          if (x == a) live = false;
+          // column a of the current matrix: stale TMEM value plus this panel's corrections
+          float colA = __uint_as_float(umma::tmem_ld1(trow + a));
+          umma::tmem_wait_ld();
+          s0[2 * s] = colA;
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            if (t < s) {
+              const float r1 = dr[t] * S.v[t][a], r2 = -dr[t] * S.u[t][a];
+              colA = fmaf(-ur[t], r1, colA);
+              colA = fmaf(-vr[t], r2, colA);
+            }
+          // pivot: largest |colA| over the unassigned rows (first occurrence)
+          float best = live ? fabsf(colA) : -1.f;
+          int bi = live ? x : 0x7fffffff;
+          float bc = colA;
+          int fl = live ? x : 0x7fffffff;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            const float oc = __shfl_xor_sync(0xffffffffu, bc, off);
+            if (ob > best || (ob == best && oi < bi)) {
+              best = ob;
+              bi = oi;
+              bc = oc;
+            }
+            fl = min(fl, __shfl_xor_sync(0xffffffffu, fl, off));
+          }
+          if (lane == 0) {
+            S.cand_a[warp] = best;
+            S.cand_i[warp] = bi;
+            S.cand_c[warp] = bc;
+            S.cand_f[warp] = fl;
+          }
+          __syncthreads();
+          float pb = S.cand_a[0], pc = S.cand_c[0];
+          int p = S.cand_i[0], pf = S.cand_f[0];
+#pragma unroll
+          for (int w = 1; w < 4; ++w) {
+            const float ob = S.cand_a[w];
+            const int oi = S.cand_i[w];
+            if (ob > pb || (ob == pb && oi < p)) {
+              pb = ob;
+              p = oi;
+              pc = S.cand_c[w];
+            }
+            pf = min(pf, S.cand_f[w]);
+          }
+          float d = -pc;
+          if (p == 0x7fffffff) {  // nothing compares (NaN column): the first live row, pivot NaN
+            p = pf;
+            d = __int_as_float(0x7fc00000);
+          }
+          const float inv = d == 0.f ? 0.f : __fdiv_rn(1.f, d);
+          if (x == p) live = false;
+          float colP = __uint_as_float(umma::tmem_ld1(trow + p));
+          umma::tmem_wait_ld();
+          s0[2 * s + 1] = colP;
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            if (t < s) {
+              const float r1 = dr[t] * S.v[t][p], r2 = -dr[t] * S.u[t][p];
+              colP = fmaf(-ur[t], r1, colP);
+              colP = fmaf(-vr[t], r2, colP);
+            }
+          ur[s] = colP * inv;
+          vr[s] = -colA * inv;
+          dr[s] = d;
+          S.u[s][x] = ur[s];
+          S.v[s][x] = vr[s];
+          if (tid == 0) {
+            const int q = S.pof[p];
+            if (q != c + 1) {
+              const int y = S.at[c + 1];
+              S.at[c + 1] = p;
+              S.at[q] = y;
+              S.pof[p] = c + 1;
+              S.pof[y] = q;
+              S.parity ^= 1;
+            }
+            S.dvec[g0 + s] = d;
+            S.pidx[2 * s] = a;
+            S.pidx[2 * s + 1] = p;
+            S.isP[a] = 1;
+            S.isP[p] = 1;
+          }
+          __syncthreads();
+        }
+      }
+      FX_TOC(tq, 9);
+      // ---- MMA operands: W[x] = (u_t, v_t), B[x] = sigma(x) d_t (v_t, -u_t)
+      {
+        const float sig = swept_before ? -1.f : 1.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int t = k >> 1;
+          float w = 0.f, z = 0.f;
+          if (t < np) {
+            w = (k & 1) ? vr[t] : ur[t];
+            z = (k & 1) ? -sig * dr[t] * ur[t] : sig * dr[t] * vr[t];
+          }
+          const uint32_t off = umma::kmajor_offset(x, k, kTcSlab) / 4;
+          const float wh = umma::tf32_round(w), zh = umma::tf32_round(z);
+          S.whi[off] = wh;
+          S.wlo[off] = umma::tf32_round(w - wh);
+          S.bhi[off] = zh;
+          S.blo[off] = umma::tf32_round(z - zh);
+        }
+      }
+      umma::fence_proxy_async_smem();
+      tc_sync();
+      FX_TOC(tq, 10);
+      if (tid == 0) {
+        const uint32_t idesc = umma::idesc_tf32(kTcN, kTcN, true);  // D -= W B^T
+#pragma unroll
+        for (int sl = 0; sl < 2; ++sl) {
+          const uint64_t ah = umma::smem_desc_kmajor(umma::smem_u32(S.whi) + sl * kTcSlab, 128, 256);
+          const uint64_t al = umma::smem_desc_kmajor(umma::smem_u32(S.wlo) + sl * kTcSlab, 128, 256);
+          const uint64_t bh = umma::smem_desc_kmajor(umma::smem_u32(S.bhi) + sl * kTcSlab, 128, 256);
+          const uint64_t bl = umma::smem_desc_kmajor(umma::smem_u32(S.blo) + sl * kTcSlab, 128, 256);
+          umma::mma_tf32(tbase, ah, bh, idesc, true);
+          umma::mma_tf32(tbase, ah, bl, idesc, true);
+          umma::mma_tf32(tbase, al, bh, idesc, true);
+        }
+        umma::mma_commit(&S.mbar);
+      }
+      __syncwarp();
+      if (!umma::mbar_wait(&S.mbar, phase, kTcWaitIters)) S.bad = 1;
+      phase ^= 1;
+      umma::fence_after_sync();
+      FX_TOC(tq, 11);
+
+      if (GRAD) {
+        // pivot rows / columns -> the block-sweep values (A = panel-start matrix):
+        //   A'_XP = A_XP A_PP^-1, A'_PP = -A_PP^-1 (16 TMEM column stores per thread),
+        //   A'_PY = A_PP^-1 A_PY = A_PP^-1 (tau(y) A_YP^T), tau = -1 unswept / +1 swept y,
+        // the latter as a second MMA whose output lanes are only the pivot rows.
+        int kx = -1;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          if (k < 2 * np && S.pidx[k] == x) kx = k;
+        if (kx >= 0) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < 2 * np) S.app[kx][j] = s0[j];
+        }
+        const unsigned notP = __ballot_sync(0xffffffffu, kx < 0);
+        if (lane == 0) S.dis[warp] = notP;
+        __syncthreads();
+        if (warp == 0) tc_block_inverse(S, np);
+        __syncthreads();
+        float pv[16];
+        const float tau = swept_before ? 1.f : -1.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float acc = 0.f, a2 = 0.f;
+          if (j < 2 * np) {
+            if (kx >= 0) {
+              acc = -S.app[kx][j];
+              a2 = S.app[kx][j];
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (i < 2 * np) acc = fmaf(s0[i], S.app[i][j], acc);
+            }
+          }
+          pv[j] = acc;
+          const float b2 = tau * s0[j];
+          const uint32_t off = umma::kmajor_offset(x, j, kTcSlab) / 4;
+          const float ah = umma::tf32_round(a2), bh = umma::tf32_round(b2);
+          S.whi[off] = ah;
+          S.wlo[off] = umma::tf32_round(a2 - ah);
+          S.bhi[off] = bh;
+          S.blo[off] = umma::tf32_round(b2 - bh);
+        }
+        umma::fence_proxy_async_smem();
+        tc_sync();
+        if (tid == 0) {
+          const uint32_t idesc = umma::idesc_tf32(kTcN, kTcN, false);
+          const uint32_t dis[4] = {S.dis[0], S.dis[1], S.dis[2], S.dis[3]};
+#pragma unroll
+          for (int sl = 0; sl < 2; ++sl) {
+            const uint64_t ah = umma::smem_desc_kmajor(umma::smem_u32(S.whi) + sl * kTcSlab, 128, 256);
+            const uint64_t al = umma::smem_desc_kmajor(umma::smem_u32(S.wlo) + sl * kTcSlab, 128, 256);
+            const uint64_t bh = umma::smem_desc_kmajor(umma::smem_u32(S.bhi) + sl * kTcSlab, 128, 256);
+            const uint64_t bl = umma::smem_desc_kmajor(umma::smem_u32(S.blo) + sl * kTcSlab, 128, 256);
+            umma::mma_tf32_masked(tbase, ah, bh, idesc, sl > 0, dis);
+            umma::mma_tf32_masked(tbase, ah, bl, idesc, true, dis);
+            umma::mma_tf32_masked(tbase, al, bh, idesc, true, dis);
+          }
+          umma::mma_commit(&S.mbar);
+        }
+        __syncwarp();
+        if (!umma::mbar_wait(&S.mbar, phase, kTcWaitIters)) S.bad = 1;
+        phase ^= 1;
+        umma::fence_after_sync();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < 2 * np) umma::tmem_st1(trow + S.pidx[j], __float_as_uint(pv[j]));
+        umma::tmem_wait_st();
+        tc_sync();
+      }
+      // the panel's pivots are swept now
+      S.isP[x] = 0;
+      __syncthreads();
+      FX_TOC(tq, 12);
+    }
+
+    // ---- (sign, logabs) from the pivots, warp 0 in a fixed order
+    if (warp == 0) {
+      float sg = 1.f;
+      KSum<float> ls;
+      ls.init();
+      int nz = 0;
+      for (int k = lane; k < npairs; k += 32) {
+        const float d = S.dvec[k];
+        sg *= d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f);
+        ls.add(logf(fabsf(d)));
+        nz += d == 0.f;
+      }
+      float lsum = ls.value();
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        sg *= __shfl_xor_sync(0xffffffffu, sg, off);
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+        nz += __shfl_xor_sync(0xffffffffu, nz, off);
+      }
+      if (lane == 0) {
+        if (S.parity) sg = -sg;
+        if (nz) sg = 0.f;
+        const float la = nz ? -INFINITY : lsum;
+        J.sign[b] = S.bad ? __int_as_float(0x7fc00000) : sg;
+        J.logabs[b] = S.bad ? __int_as_float(0x7fc00000) : la;
+        if (J.value) J.value[b] = sg * expf(la);
+        S.cand_f[0] = nz;  // reused below as the singular flag
+      }
+    }
+    __syncthreads();
+    if (GRAD) {
+      // TMEM = -S^-1: gradient of sum(logabs) = -S^-1 / 2, scaled by coef; 32-row chunks
+      // staged through shared memory for coalesced stores
+      const bool zero = S.cand_f[0] != 0 || S.bad;
+      const float f = 0.5f * (J.coef ? J.coef[b] : 1.f);
+      float* G = J.g + b * (int64_t)n * n;
+      float* stage = S.whi;
+      for (int r0 = 0; r0 < n; r0 += 32) {
+        if (warp == (r0 >> 5)) {
+          for (int c0 = 0; c0 < kTcN; c0 += 8) {
+            uint32_t vals[8];
+            umma::tmem_ld8(trow + c0, vals);
+            umma::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) stage[lane * kStageLd + c0 + j] = zero ? 0.f : f * __uint_as_float(vals[j]);
+          }
+        }
+        __syncthreads();
+        const int rows = min(32, n - r0);
+        for (int idx = tid; idx < rows * n; idx += 128) {
+          const int r = idx / n, c = idx - r * n;
+          G[(r0 + r) * n + c] = stage[r * kStageLd + c];
+        }
+        __syncthreads();
+      }
+    }
+    tc_sync();
+    FX_TOC(tq, 13);
+  }
+  if (warp == 0) umma::tmem_dealloc(tbase, kTcN);
+}
+
+}  // namespace fx

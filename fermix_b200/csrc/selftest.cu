@@ -15,7 +15,7 @@ constexpr int kM = 128, kN = 128, kK = 16;
 constexpr uint32_t kSlab = kM * 8 * 4;  // bytes of one K = 8 slab of a 128-row operand
 
 __global__ void __launch_bounds__(128) umma_selftest_kernel(const float* A, const float* B, const float* C, float* D,
-                                                            int negate, int* status) {
+                                                            int negate, int accumulate, uint4 dis, int* status) {
   __shared__ __align__(1024) float sAhi[kM * kK], sAlo[kM * kK], sBhi[kN * kK], sBlo[kN * kK];
   __shared__ uint32_t tslot;
   __shared__ __align__(8) uint64_t mbar;
@@ -54,14 +54,15 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const float* A, cons
   fence_after_sync();
   if (tid == 0) {
     const uint32_t idesc = idesc_tf32(kM, kN, negate != 0);
+    const uint32_t m4[4] = {dis.x, dis.y, dis.z, dis.w};
     for (int s = 0; s < kK / 8; ++s) {
       const uint64_t ahi = smem_desc_kmajor(smem_u32(sAhi) + s * kSlab, 128, 256);
       const uint64_t alo = smem_desc_kmajor(smem_u32(sAlo) + s * kSlab, 128, 256);
       const uint64_t bhi = smem_desc_kmajor(smem_u32(sBhi) + s * kSlab, 128, 256);
       const uint64_t blo = smem_desc_kmajor(smem_u32(sBlo) + s * kSlab, 128, 256);
-      mma_tf32(tbase, ahi, bhi, idesc, true);
-      mma_tf32(tbase, ahi, blo, idesc, true);
-      mma_tf32(tbase, alo, bhi, idesc, true);
+      mma_tf32_masked(tbase, ahi, bhi, idesc, accumulate != 0 || s > 0, m4);
+      mma_tf32_masked(tbase, ahi, blo, idesc, true, m4);
+      mma_tf32_masked(tbase, alo, bhi, idesc, true, m4);
     }
     mma_commit(&mbar);
   }
@@ -83,8 +84,10 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const float* A, cons
 }  // namespace
 
 extern "C" int fermix_selftest_umma(void* stream, const float* a, const float* b, const float* c, float* d, int negate,
-                                    int* status) {
+                                    int accumulate, const unsigned* disable_lanes, int* status) {
   if (!a || !b || !c || !d || !status) return FX_ERR_NULL;
-  umma_selftest_kernel<<<1, 128, 0, static_cast<cudaStream_t>(stream)>>>(a, b, c, d, negate, status);
+  uint4 dis = make_uint4(0, 0, 0, 0);
+  if (disable_lanes) dis = make_uint4(disable_lanes[0], disable_lanes[1], disable_lanes[2], disable_lanes[3]);
+  umma_selftest_kernel<<<1, 128, 0, static_cast<cudaStream_t>(stream)>>>(a, b, c, d, negate, accumulate, dis, status);
   return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
 }

@@ -100,11 +100,13 @@ int fermix_check_prec(int dtype, int prec);
 const char* fermix_strerror(int code);
 
 /* Self-test of the tensor-core path on the current GPU (no reference counterpart): one
- * 128 x 128 x 16 update d = c + (negate ? -1 : 1) * a b^T computed with tcgen05 3xTF32 MMAs
- * into tensor memory, all operands row-major float32 (a, b: 128 x 16; c, d: 128 x 128).
- * *status gets bit 0 set if the MMA completion wait timed out. */
+ * 128 x 128 x 16 update d = (accumulate ? c : 0) + (negate ? -1 : 1) * a b^T computed with
+ * tcgen05 3xTF32 MMAs into tensor memory, all operands row-major float32 (a, b: 128 x 16;
+ * c, d: 128 x 128; device pointers). disable_lanes (host array of 4 words, or NULL): bit l
+ * of word w keeps row 32 w + l of d equal to c. *status (device) gets bit 0 set if the
+ * MMA completion wait timed out. */
 int fermix_selftest_umma(void* stream, const float* a, const float* b, const float* c, float* d, int negate,
-                         int* status);
+                         int accumulate, const unsigned* disable_lanes, int* status);
 
 /* Library version, major * 10000 + minor * 100 + patch. */
 int fermix_version(void);

@@ -13,15 +13,18 @@ from tests.helpers import cuda, host, jgrad
 pytestmark = pytest.mark.gpu
 
 
-def assert_grad_parity(g, g64, g_ref32, floor=1e-3):
+def assert_grad_parity(g, g64, g_ref32, mats, floor=1e-3):
     """Per matrix: |g - g64| / |g64| within max(floor, 4x the error of the reference's own
-    single-precision path (the oracle run in float32) on the same input) -- random
-    matrices of this size have condition numbers up to ~1e5, where no float32 algorithm
-    stays inside a fixed 1e-3."""
+    single-precision path (the oracle run in float32), cond(A) * eps_f32) -- random
+    matrices of this size reach condition numbers ~1e5, where a float32 inverse is only
+    good to about cond * eps, and the error of any one elimination order varies by an
+    order of magnitude inside that bound."""
+    eps = np.finfo(np.float32).eps
     for i in range(len(g64)):
         mine = relerr(g[i], g64[i])
         ref = relerr(g_ref32[i], g64[i])
-        assert mine <= max(floor, 4 * ref), (i, mine, ref)
+        cond = np.linalg.cond(mats[i].astype(np.float64))
+        assert mine <= max(floor, 4 * ref, cond * eps), (i, mine, ref, cond)
 
 
 def test_c1_slogdet_f32_n128():
@@ -46,7 +49,7 @@ def test_c2_slogpf_f32_n128_fwd_and_vjp(prec):
     assert np.array_equal(s, so)
     assert np.max(np.abs(l - lo)) < 1e-4 * max(1.0, np.abs(lo).max())
     g64 = oracle.slogpf_grad(S.astype(np.float64))
-    assert_grad_parity(g, g64, oracle.slogpf_grad(S))
+    assert_grad_parity(g, g64, oracle.slogpf_grad(S), S)
 
 
 def _qmc_batch(B, dup_frac, seed):
@@ -79,7 +82,7 @@ def test_c3_qmc_slogdet_f32_n256_duplicate_rows_are_exactly_singular():
     assert np.array_equal(s[reg], s64.astype(np.float32))
     assert np.max(np.abs(l[reg] - l64)) < 1e-4 * max(1.0, np.abs(l64).max())
     inv = np.swapaxes(np.linalg.inv(ref64(A[reg])), -1, -2)
-    assert_grad_parity(g[reg], inv, oracle.slogdet_grad(A[reg]))
+    assert_grad_parity(g[reg], inv, oracle.slogdet_grad(A[reg]), A[reg])
 
 
 def test_c4_slogpf_c64_n512_fwd_and_grad():
