@@ -362,6 +362,71 @@ const char* fermix_strerror(int code) {
 
 int fermix_version(void) { return 100; }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------- static-scratch variant
+// fermix_slogdet_grad_static: fermix_slogdet_grad whose LU kernels take their matrix
+// slots (factor + inverse, 2 n^2 elements per resident block, used only when a matrix
+// does not fit in one block's shared memory) from the fixed device array below instead
+// of a caller workspace. It is for callers that cannot allocate device memory when they
+// call: a host framework whose allocator owns all device memory and hands the op no
+// scratch operand, or a latency-bound loop where cudaMalloc / cudaFree would synchronise
+// the device. Nothing in the slots has to start at zero: the kernels write every element
+// of a slot (the matrix load, then the column-by-column inverse) before reading it, so
+// the array is never cleared. The array is shared by every call on a device: two calls
+// in flight at once on one device (different streams or host threads) race on it and
+// must be serialised by the caller (one stream, or an event between them).
+static __device__ __align__(256) unsigned char fx_static_scratch[FX_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+void* g_scratch_ptr[kMaxDevices];
+std::once_flag g_scratch_once[kMaxDevices];
+
+// Device address of fx_static_scratch on the current device, looked up once per device
+// with that device current (nullptr if the lookup failed). The lookup may load this
+// module on the device, so the first call on each device belongs before any stream
+// capture.
+void* static_scratch() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::call_once(g_scratch_once[dev], [dev]() {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, fx_static_scratch) == cudaSuccess) {
+      g_scratch_ptr[dev] = p;
+    } else {
+      g_scratch_ptr[dev] = nullptr;
+      (void)cudaGetLastError();  // clear the error state so later calls report their own errors
+    }
+  });
+  return g_scratch_ptr[dev];
+}
+
+}  // namespace
+
+extern "C" {
+
+int fermix_slogdet_grad_static(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a,
+                               const void* coef, int conj_out, int adjugate, void* sign, void* logabs, void* value,
+                               void* grad) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (batch == 0) return FX_OK;
+  if ((!a && n > 0) || !sign || !logabs || (!grad && n > 0)) return FX_ERR_NULL;
+  // one matrix slot must fit: the workspace a single-member batch needs is one slot
+  const size_t slot = fermix_workspace_bytes(FX_OP_SLOGDET, dtype, 1, n, 1);
+  if (slot > (size_t)FX_STATIC_SCRATCH_BYTES) return FX_ERR_WORKSPACE;
+  void* scratch = static_scratch();
+  if (!scratch) return FX_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_det<T>(s, batch, n, a, coef, conj_out, mode, sign, logabs, value, grad, scratch,
+                      (size_t)FX_STATIC_SCRATCH_BYTES);
+  });
+}
+
 #ifdef FX_PHASE_TIMERS
 // profiling builds only: copy out / reset the per-phase cycle counters
 int fermix_debug_phase_cycles(unsigned long long* out, int reset) {

@@ -89,6 +89,29 @@ int fermix_slogpf_grad(void* stream, int dtype, int prec, int64_t batch, int64_t
                        const void* a, const void* coef, int conj_out, int adjugate, void* sign, void* logabs,
                        void* value, void* grad, void* workspace, size_t workspace_bytes);
 
+/* Size of the fixed device array fermix_slogdet_grad_static uses instead of a workspace
+ * (16 MiB, one copy per device, part of the library's device image). */
+#define FX_STATIC_SCRATCH_BYTES (16u << 20)
+
+/* fermix_slogdet_grad without a workspace argument (no reference counterpart): the LU
+ * kernels take their per-block matrix slots from a fixed device array of
+ * FX_STATIC_SCRATCH_BYTES instead of caller memory, and the call allocates nothing. For
+ * callers that cannot allocate device memory when they call: a host framework whose
+ * allocator owns the device and passes the op no scratch operand, or a latency-bound loop
+ * where cudaMalloc / cudaFree would synchronise the device.
+ * Limit: one slot (2 n^2 elements, needed when a matrix does not fit in one block's shared
+ * memory) must fit in the array -- n <= 1448 (float32), 1024 (float64, complex64), 724
+ * (complex128); larger n returns FX_ERR_WORKSPACE. Fewer slots than resident blocks means
+ * fewer blocks in flight, so large-n calls run slower than fermix_slogdet_grad with a full
+ * workspace. Results are bit-identical to fermix_slogdet_grad.
+ * The array is shared by all calls on a device: calls that overlap in time on one device
+ * (different streams or host threads) race on it; serialise them. The first call on each
+ * device looks the array up (cudaGetSymbolAddress) and should come before any stream
+ * capture. */
+int fermix_slogdet_grad_static(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a,
+                               const void* coef, int conj_out, int adjugate, void* sign, void* logabs, void* value,
+                               void* grad);
+
 /* Workspace bytes a call needs on the current device (0 when every matrix fits in one
  * block's shared memory); grad != 0 for the *_grad entry points. */
 size_t fermix_workspace_bytes(int op, int dtype, int64_t batch, int64_t n, int grad);
