@@ -18,6 +18,7 @@
 #include "poly.cuh"
 #include "small.cuh"
 #include "pf_tc.cuh"
+#include "lu_tc.cuh"
 
 namespace {
 
@@ -145,6 +146,31 @@ int launch_pf_tc(cudaStream_t s, Job<float> J) {
   return FX_OK;
 }
 
+// Tensor-core slogdet (float32, prec tf32x3, 8 <= n <= 128, forward or slogdet gradient):
+// same residency scheme as the Pfaffian kernel above.
+constexpr size_t kLuTcSmem = 54 * 1024;  // at most four blocks per SM (4 x 55 KB)
+static_assert(sizeof(LuTcSmem) <= kLuTcSmem, "LuTcSmem too large");
+
+bool use_lu_tc(int dtype_is_f32, int prec, int n, int mode) {
+  return dtype_is_f32 && prec != FX_PREC_IEEE && n >= 8 && n <= kTcN && (mode == MODE_FWD || mode == MODE_SLOG_GRAD);
+}
+
+int launch_lu_tc(cudaStream_t s, Job<float> J) {
+  const DevInfo* D = dev_info();
+  if (!D) return FX_ERR_DEVICE;
+  void* k = J.mode == MODE_FWD ? (void*)&lu_tc_kernel<false> : (void*)&lu_tc_kernel<true>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLuTcSmem) != cudaSuccess)
+    return FX_ERR_CUDA;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    return FX_ERR_CUDA;
+  const int64_t cap = (int64_t)D->sms * 4;
+  const int64_t grid = J.B < cap ? J.B : cap;
+  if (grid < 1) return FX_OK;
+  void* args[] = {&J};
+  if (cudaLaunchKernel(k, dim3((unsigned)grid), dim3(128), args, kLuTcSmem, s) != cudaSuccess) return FX_ERR_CUDA;
+  return FX_OK;
+}
+
 template <typename T, bool PF>
 int launch_fused(cudaStream_t s, Job<T> J, void* ws, size_t ws_bytes) {
   Plan P;
@@ -195,10 +221,23 @@ Job<T> make_job(int64_t batch, int64_t n, const void* a, const void* coef, int c
 }
 
 template <typename T>
-int run_det(cudaStream_t s, int64_t batch, int64_t n, const void* a, const void* coef, int conj_out, int mode,
-            void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb) {
+int run_det(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* a, const void* coef, int conj_out,
+            int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb) {
   Job<T> J = make_job<T>(batch, n, a, coef, conj_out, 0, mode, sign, logabs, value, grad);
   if (n <= DET_POLY_MAX) return launch_poly<T>(s, J, 0);
+  if constexpr (std::is_same<T, float>::value) {
+    if (use_lu_tc(1, prec, (int)n, mode)) return launch_lu_tc(s, J);
+    if (mode == MODE_VALUE_GRAD && use_lu_tc(1, prec, (int)n, MODE_FWD)) {
+      // the adjugate comes from the register-panel kernel; (sign, logabs, value) are
+      // rewritten by the tensor-core forward (same stream) to equal fermix_slogdet's bits
+      int e = launch_fused<T, false>(s, J, ws, wsb);
+      if (e) return e;
+      Job<T> F = J;
+      F.mode = MODE_FWD;
+      F.g = nullptr;
+      return launch_lu_tc(s, F);
+    }
+  }
   return launch_fused<T, false>(s, J, ws, wsb);
 }
 
@@ -278,7 +317,7 @@ int fermix_slogdet(void* stream, int dtype, int prec, int64_t batch, int64_t n, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
-    return run_det<T>(s, batch, n, a, nullptr, 0, MODE_FWD, sign, logabs, value, nullptr, workspace,
+    return run_det<T>(s, prec, batch, n, a, nullptr, 0, MODE_FWD, sign, logabs, value, nullptr, workspace,
                       workspace_bytes);
   });
 }
@@ -294,7 +333,7 @@ int fermix_slogdet_grad(void* stream, int dtype, int prec, int64_t batch, int64_
   const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
-    return run_det<T>(s, batch, n, a, coef, conj_out, mode, sign, logabs, value, grad, workspace, workspace_bytes);
+    return run_det<T>(s, prec, batch, n, a, coef, conj_out, mode, sign, logabs, value, grad, workspace, workspace_bytes);
   });
 }
 
@@ -422,7 +461,7 @@ int fermix_slogdet_grad_static(void* stream, int dtype, int prec, int64_t batch,
   const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
-    return run_det<T>(s, batch, n, a, coef, conj_out, mode, sign, logabs, value, grad, scratch,
+    return run_det<T>(s, prec, batch, n, a, coef, conj_out, mode, sign, logabs, value, grad, scratch,
                       (size_t)FX_STATIC_SCRATCH_BYTES);
   });
 }

@@ -22,13 +22,9 @@
 // the swept index sets, symmetric across them.
 #pragma once
 #include "fused_lu.cuh"
-#include "umma.cuh"
+#include "tc_common.cuh"
 
 namespace fx {
-
-constexpr int kTcN = 128;                        // TMEM lanes / columns of the matrix
-constexpr uint32_t kTcSlab = kTcN * 8 * 4;       // bytes of one K = 8 operand slab
-constexpr uint32_t kTcWaitIters = 1u << 26;       // bounded MMA completion wait
 
 struct PfTcSmem {
   float u[8][kTcN];  // u_t[x] = col_p[x] / d_t of the panel's pairs (broadcast reads)
@@ -47,12 +43,6 @@ struct PfTcSmem {
   int parity, bad;
   uint64_t mbar;
 };
-
-__device__ __forceinline__ void tc_sync() {
-  umma::fence_before_sync();
-  __syncthreads();
-  umma::fence_after_sync();
-}
 
 // Inverse of the m x m (m = 2 np <= 16) pivot block in S.app by sequential 2 x 2 pair
 // sweeps (pairs (2q, 2q+1)); warp 0, lane k owns row k. Result: S.app = A_PP^-1.
@@ -102,18 +92,6 @@ __device__ void tc_block_inverse(PfTcSmem& S, int np) {
   }
 }
 
-constexpr int kStageLd = kTcN + 1;  // staged rows: odd stride, conflict-free row reads
-
-// Rows r0 .. r0+31 of the n x n row-major matrix src into stage (stride kStageLd), zero
-// outside n x n; coalesced over the block.
-__device__ __forceinline__ void tc_stage_rows(float* stage, const float* src, int n, int r0) {
-  for (int idx = threadIdx.x; idx < 32 * kTcN; idx += blockDim.x) {
-    const int r = idx >> 7, c = idx & (kTcN - 1);
-    const int row = r0 + r;
-    stage[r * kStageLd + c] = (row < n && c < n) ? __ldg(src + row * n + c) : 0.f;
-  }
-}
-
 template <bool GRAD>
 __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -139,45 +117,11 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
 
   for (int64_t b = blockIdx.x; b < J.B; b += gridDim.x) {
     FX_TIC(tq);
-    // ---- the (skew-symmetrised) matrix into TMEM, zero outside n x n: 32-row chunks
-    // staged through shared memory (coalesced global reads, conflict-free row reads)
+    // ---- the (skew-symmetrised) matrix into TMEM, zero outside n x n; the block's
+    // next matrix starts streaming into L2 meanwhile
     const float* src = J.a + b * (int64_t)n * n;
-    float* stage = S.whi;  // 32 x kStageLd floats, spans the (idle) operand buffers
-    for (int r0 = 0; r0 < kTcN; r0 += 32) {
-      tc_stage_rows(stage, src, n, r0);
-      __syncthreads();
-      if (warp == (r0 >> 5)) {
-        for (int c0 = 0; c0 < kTcN; c0 += 8) {
-          uint32_t vals[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) vals[j] = __float_as_uint(stage[lane * kStageLd + c0 + j]);
-          umma::tmem_st8(trow + c0, vals);
-        }
-        umma::tmem_wait_st();
-      }
-      __syncthreads();
-    }
-    if (J.skew) {
-      // S = (A - A^T) / 2: the rows of chunk r0 are the columns r0..r0+31 of A^T
-      umma::fence_before_sync();
-      for (int r0 = 0; r0 < kTcN; r0 += 32) {
-        tc_stage_rows(stage, src, n, r0);
-        __syncthreads();
-        umma::fence_after_sync();
-        for (int c0 = r0; c0 < r0 + 32; c0 += 8) {
-          uint32_t vals[8];
-          umma::tmem_ld8(trow + c0, vals);
-          umma::tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            vals[j] = __float_as_uint((__uint_as_float(vals[j]) - stage[(c0 + j - r0) * kStageLd + x]) * 0.5f);
-          umma::tmem_st8(trow + c0, vals);
-        }
-        umma::tmem_wait_st();
-        umma::fence_before_sync();
-        __syncthreads();
-      }
-    }
+    if (tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
+    tc_load_matrix(src, n, J.skew != 0, trow, x);
     S.at[x] = x;
     S.pof[x] = x;
     S.isP[x] = 0;
@@ -444,30 +388,10 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
     }
     __syncthreads();
     if (GRAD) {
-      // TMEM = -S^-1: gradient of sum(logabs) = -S^-1 / 2, scaled by coef; 32-row chunks
-      // staged through shared memory for coalesced stores
+      // TMEM = -S^-1: gradient of sum(logabs) = -S^-1 / 2, scaled by coef
       const bool zero = S.cand_f[0] != 0 || S.bad;
       const float f = 0.5f * (J.coef ? J.coef[b] : 1.f);
-      float* G = J.g + b * (int64_t)n * n;
-      float* stage = S.whi;
-      for (int r0 = 0; r0 < n; r0 += 32) {
-        if (warp == (r0 >> 5)) {
-          for (int c0 = 0; c0 < kTcN; c0 += 8) {
-            uint32_t vals[8];
-            umma::tmem_ld8(trow + c0, vals);
-            umma::tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 8; ++j) stage[lane * kStageLd + c0 + j] = zero ? 0.f : f * __uint_as_float(vals[j]);
-          }
-        }
-        __syncthreads();
-        const int rows = min(32, n - r0);
-        for (int idx = tid; idx < rows * n; idx += 128) {
-          const int r = idx / n, c = idx - r * n;
-          G[(r0 + r) * n + c] = stage[r * kStageLd + c];
-        }
-        __syncthreads();
-      }
+      tc_store_rows(J.g + b * (int64_t)n * n, n, f, zero, trow, x);
     }
     tc_sync();
     FX_TOC(tq, 13);
