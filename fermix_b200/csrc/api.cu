@@ -148,7 +148,7 @@ int launch_pf_tc(cudaStream_t s, Job<float> J) {
 
 // Tensor-core slogdet (float32, prec tf32x3, 8 <= n <= 128, forward or slogdet gradient):
 // same residency scheme as the Pfaffian kernel above.
-constexpr size_t kLuTcSmem = 54 * 1024;  // at most four blocks per SM (4 x 55 KB)
+constexpr size_t kLuTcSmem = 55 * 1024;  // at most four blocks per SM (4 x 56 KB)
 static_assert(sizeof(LuTcSmem) <= kLuTcSmem, "LuTcSmem too large");
 
 bool use_lu_tc(int dtype_is_f32, int prec, int n, int mode) {

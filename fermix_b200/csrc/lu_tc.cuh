@@ -12,8 +12,9 @@
 // stays in TMEM (128 columns) for the whole call and rows are never moved (virtual
 // pivoting). Per panel of 16 columns:
 //   1. every row reads its 16 panel entries into registers and the panel is factored
-//      there: per column one warp argmax, one block barrier (each warp's candidate row
-//      travels with its candidate value), then every other row eliminates;
+//      there: per column a two-instruction warp argmax (redux.sync on a packed |value|
+//      key, then on the row index), ONE block barrier (each warp's candidate row
+//      travels with its key), then every other row eliminates;
 //   2. with P the panel's pivot rows, K its columns and l_x row x's multipliers, the
 //      block exchange of (P, K) is ONE rank-16 tensor-core update D -= C B^T:
 //        C_x = l_x L11^-1            (x not in P; back substitution, so that a row equal
@@ -22,8 +23,9 @@
 //        B_y = A_{P,y} (y not in K), B_{K_t} = -e_t,
 //      after the K columns are preset to 0 (rows not in P) / -e_j (row P_j). Sweeping all
 //      panels leaves TMEM[p_s][t] = (A^-1)[s][p_t], p_s the row pivoted at step s. The
-//      forward-only mode skips the presets and the pivot-row coefficients; the rows not
-//      yet pivoted evolve identically, so its (sign, logabs) are bit-identical.
+//      forward-only mode skips the presets, the pivot-row coefficients and the rows
+//      pivoted earlier; the rows not yet pivoted evolve identically, so its
+//      (sign, logabs) are bit-identical.
 // B is split three ways (hi + mid + lo == value exactly) and the update uses the
 // products hi*hi + hi*mid + hi*lo + lo*hi: a row that duplicates a pivot row therefore
 // cancels to exact zeros, and duplicated rows give an exactly zero pivot as in the
@@ -34,28 +36,23 @@
 
 namespace fx {
 
-struct __align__(16) LuTcCand {
-  float absv;     // candidate |value| (-1: no candidate in this warp)
-  int idx;        // candidate row
-  unsigned live;  // ballot of this warp's rows not yet pivoted
-  int pad;
-  float row[16];  // the candidate's current panel entries
-};
-
 constexpr int kProwLd = kTcN + 4;  // staged pivot rows: 16-byte rows, conflict-free column reads
 
 struct LuTcSmem {
-  float chi[kTcN * 16], clo[kTcN * 16];                   // A operand C, K-major, TF32 hi / lo
+  float chi[kTcN * 16], clo[kTcN * 16];  // A operand C, K-major, TF32 hi / lo
   float bhi[kTcN * 16], bmid[kTcN * 16], blo[kTcN * 16];  // B operand, K-major, exact 3-way split
-  float prow[16][kProwLd];                                // the panel's pivot rows (TMEM values)
-  LuTcCand cand[2][4];                                    // per-warp candidates, by step parity
-  float L11[16][17];                                      // panel multipliers of the pivot rows
-  float U11[16][17];                                      // panel pivot rows (gradient mode)
-  float dvec[kTcN];                                       // pivots
-  int at[kTcN];                                           // pivot position -> row
-  int wpar[4];                                            // per-warp parity of inversions
+  uint4 chead[2][4];        // per-warp pivot candidates by step parity: key, row, live ballot
+  float crow[2][4][16];     // the candidates' current panel entries
+  float prow[16][kProwLd];  // the panel's pivot rows (TMEM values)
+  float L11[16][17];        // multipliers of the pivot rows (strict lower part)
+  float U11[16][17];        // the pivot rows' panel entries (upper part)
+  float Linv[16][17];       // L11^-1 (gradient mode)
+  float Uinv[16][17];       // U11^-1 (gradient mode)
+  float dvec[kTcN];         // pivots
+  int at[kTcN];             // pivot position -> row
+  int wpar[4];              // per-warp parity of the inversions
   uint32_t tslot;
-  int bad;
+  int bad, nz;
   uint64_t mbar;
 };
 
@@ -67,8 +64,16 @@ __device__ __forceinline__ void split3(float v, float& hi, float& mid, float& lo
   lo = r - mid;
 }
 
+// Order key of a pivot candidate: 0 = not a candidate, 1 = NaN (a candidate only when
+// every candidate is NaN), else |v| ordered as its bit pattern, shifted above 1.
+__device__ __forceinline__ unsigned piv_key(float v, bool live) {
+  if (!live) return 0u;
+  if (v != v) return 1u;
+  return __float_as_uint(fabsf(v)) + 2u;
+}
+
 template <bool GRAD>
-__global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
+__global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   LuTcSmem& S = *reinterpret_cast<LuTcSmem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -88,13 +93,15 @@ __global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
   uint32_t phase = 0;
 
   for (int64_t b = blockIdx.x; b < J.B; b += gridDim.x) {
+    FX_TIC(tq);
     const float* src = J.a + b * (int64_t)n * n;
     if (tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
     tc_load_matrix(src, n, false, trow, x);
     int mypos = x < n ? -1 : kTcN;  // pivot position of this row (-1: not yet pivoted)
-    int myinv = 0;                  // rows of smaller index still unpivoted when this one was
+    int myinv = 0;                  // parity of the inversions this row adds as a pivot
     if (tid == 0) S.bad = 0;
     tc_sync();
+    FX_TOC(tq, 0);
 
     for (int k0 = 0; k0 < n; k0 += 16) {
       const int kw = min(16, n - k0);
@@ -112,56 +119,35 @@ __global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
 #pragma unroll
         for (int t = 0; t < 16; ++t) lr[t] = 0.f;
       }
-      // ---- panel factorisation in registers
+      // ---- panel factorisation in registers, one block barrier per column
 #pragma unroll
       for (int s = 0; s < 16; ++s) {
         if (s < kw) {
           const bool live = mypos < 0;
           const float v = pr[s];
-          float best = live ? (v != v ? -0.5f : fabsf(v)) : -1.f;  // NaN: live, never preferred
-          int bi = live ? x : 0x7fffffff;
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) {
-            const float ob = __shfl_xor_sync(0xffffffffu, best, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            if (ob > best || (ob == best && oi < bi)) {
-              best = ob;
-              bi = oi;
-            }
-          }
+          const unsigned key = piv_key(v, live);
+          const unsigned km = __reduce_max_sync(0xffffffffu, key);
+          const int wi = __reduce_min_sync(0xffffffffu, key == km ? x : 0x7fffffff);
           const unsigned lm = __ballot_sync(0xffffffffu, live);
-          LuTcCand& mine = S.cand[s & 1][warp];
-          if (x == bi) {
-            mine.absv = best;
-            mine.idx = bi;
-            float4* r4 = reinterpret_cast<float4*>(mine.row);
+          if (x == wi) {
+            // this warp's candidate (key 0: the warp has no unpivoted row left)
+            S.chead[s & 1][warp] = make_uint4(km, (unsigned)wi, lm, 0u);
+            float4* r4 = reinterpret_cast<float4*>(S.crow[s & 1][warp]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) r4[q] = make_float4(pr[4 * q], pr[4 * q + 1], pr[4 * q + 2], pr[4 * q + 3]);
           }
-          if (lane == 0) {
-            mine.live = lm;
-            if (bi == 0x7fffffff) {
-              mine.absv = -1.f;
-              mine.idx = 0x7fffffff;
-            }
-          }
           __syncthreads();
-          int pw = 0;
-          float pb = S.cand[s & 1][0].absv;
-          int p = S.cand[s & 1][0].idx;
+          uint4 hd[4];
 #pragma unroll
-          for (int w = 1; w < 4; ++w) {
-            const float ob = S.cand[s & 1][w].absv;
-            const int oi = S.cand[s & 1][w].idx;
-            if (ob > pb || (ob == pb && oi < p)) {
-              pb = ob;
-              p = oi;
-              pw = w;
-            }
-          }
+          for (int w = 0; w < 4; ++w) hd[w] = S.chead[s & 1][w];
+          int pw = 0;
+#pragma unroll
+          for (int w = 1; w < 4; ++w)
+            if (hd[w].x > hd[pw].x || (hd[w].x == hd[pw].x && hd[w].y < hd[pw].y)) pw = w;
+          const int p = (int)(pw == 0 ? hd[0].y : pw == 1 ? hd[1].y : pw == 2 ? hd[2].y : hd[3].y);
           float ur[16];
           {
-            const float4* r4 = reinterpret_cast<const float4*>(S.cand[s & 1][pw].row);
+            const float4* r4 = reinterpret_cast<const float4*>(S.crow[s & 1][pw]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const float4 t = r4[q];
@@ -174,21 +160,17 @@ __global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
           const float piv = ur[s];
           if (x == p) {
             mypos = k0 + s;
-            int cnt = __popc(S.cand[s & 1][warp].live & ((1u << lane) - 1u));
+            // rows of smaller index still unpivoted: the inversions this pivot adds
+            int cnt = __popc(hd[warp].z & ((1u << lane) - 1u));
 #pragma unroll
             for (int w = 0; w < 4; ++w)
-              if (w < warp) cnt += __popc(S.cand[s & 1][w].live);
-            myinv = cnt & 1;
+              if (w < warp) cnt += __popc(hd[w].z);
+            myinv ^= cnt & 1;
             S.dvec[k0 + s] = piv;
             S.at[k0 + s] = x;
-#pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              if (t < s) S.L11[s][t] = lr[t];
-              if (GRAD && t >= s) S.U11[s][t] = pr[t];
-            }
-          } else if (x < n && mypos < k0) {
-            // every row outside this panel's pivots eliminates (rows pivoted in earlier
-            // panels too: gradient mode needs their multipliers)
+          } else if (x < n && (GRAD ? mypos < k0 : mypos < 0)) {
+            // rows outside this panel's pivots eliminate (gradient mode: rows pivoted in
+            // earlier panels too, for their multipliers)
             const float l = piv == 0.f ? 0.f : __fdiv_rn(v, piv);
             lr[s] = l;
 #pragma unroll
@@ -197,13 +179,52 @@ __global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
           }
         }
       }
+      const bool inP = mypos >= k0 && mypos < k0 + kw;
+      if (inP) {
+        // a pivot row keeps its multipliers (L11 row) and its remaining entries (U11 row)
+        const int j = mypos - k0;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          if (t < j) S.L11[j][t] = lr[t];
+          else if (GRAD) S.U11[j][t] = pr[t];
+        }
+      }
       __syncthreads();  // L11 / U11 / at complete
-      const bool inP = mypos >= k0 && mypos < kTcN;
-      // ---- the pivot rows' current TMEM values into prow (warps holding pivot rows)
+      FX_TOC(tq, 1);
+      if (GRAD) {
+        // L11^-1 by columns (warp 2) and U11^-1 by rows (warp 3), lanes < kw
+        if (warp == 2 && lane < kw) {
+          const int t = lane;
+          float y[16];
+#pragma unroll
+          for (int r = 0; r < 16; ++r) {
+            float acc = r == t ? 1.f : 0.f;
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              if (q < r) acc = fmaf(-S.L11[r][q], y[q], acc);
+            y[r] = (r >= t && r < kw) ? acc : 0.f;
+            S.Linv[r][t] = y[r];
+          }
+        } else if (warp == 3 && lane < kw) {
+          const int j = lane;
+          float w[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            float acc = t == j ? 1.f : 0.f;
+#pragma unroll
+            for (int r = 0; r < 16; ++r)
+              if (r < t) acc = fmaf(-w[r], S.U11[r][t], acc);
+            w[t] = (t >= j && t < kw) ? __fdiv_rn(acc, S.U11[t][t]) : 0.f;
+            S.Uinv[j][t] = w[t];
+          }
+        }
+      }
+      // ---- the pivot rows' current TMEM values into prow (warps holding pivot rows;
+      // forward mode: trailing columns only)
       if (__ballot_sync(0xffffffffu, inP) != 0u) {
         const int tp = mypos - k0;
 #pragma unroll 1
-        for (int c0 = 0; c0 < kTcN; c0 += 32) {
+        for (int c0 = GRAD ? 0 : ((k0 + kw) & ~31); c0 < kTcN; c0 += 32) {
           uint32_t w[32];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -222,47 +243,33 @@ __global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
           }
         }
       }
-
-      // ---- coefficients C_x (A operand), K-major, hi / lo
+      // ---- coefficients of the rows outside P: C_x L11 = l_x by back substitution
+      // (increasing r inside each sum)
       float c[16];
 #pragma unroll
       for (int t = 0; t < 16; ++t) c[t] = 0.f;
-      if (x < n) {
-        if (inP) {
-          if (GRAD) {
-            // row j of A_PK^-1 = (e_j U11^-1) L11^-1, then + e_j
-            const int j = mypos - k0;
-            float w[16];
+      if (x < n && !inP && (GRAD || mypos < 0)) {
 #pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              float acc = (t == j) ? 1.f : 0.f;
+        for (int t = 15; t >= 0; --t) {
+          float acc = lr[t];
 #pragma unroll
-              for (int r = 0; r < 16; ++r)
-                if (r < t) acc = fmaf(-w[r], S.U11[r][t], acc);
-              w[t] = (t < kw && t >= j) ? __fdiv_rn(acc, S.U11[t][t]) : 0.f;
-            }
+          for (int r = 0; r < 16; ++r)
+            if (r > t && r < kw) acc = fmaf(-c[r], S.L11[r][t], acc);
+          c[t] = t < kw ? acc : 0.f;
+        }
+      }
+      FX_TOC(tq, 2);
+      __syncthreads();  // prow, Linv, Uinv complete; the panel buffer is free
+      if (GRAD && inP) {
+        // row j of A_PK^-1 = U11^-1 L11^-1, then + e_j
+        const int j = mypos - k0;
 #pragma unroll
-            for (int t = 15; t >= 0; --t) {
-              float acc = w[t];
+        for (int t = 0; t < 16; ++t) {
+          float acc = t == j ? 1.f : 0.f;
 #pragma unroll
-              for (int r = 0; r < 16; ++r)
-                if (r > t && r < kw) acc = fmaf(-c[r], S.L11[r][t], acc);
-              c[t] = t < kw ? acc : 0.f;
-            }
-#pragma unroll
-            for (int t = 0; t < 16; ++t)
-              if (t == j) c[t] += 1.f;
-          }
-        } else if (GRAD || mypos < 0) {
-          // C_x L11 = l_x, by back substitution (increasing r inside each sum)
-#pragma unroll
-          for (int t = 15; t >= 0; --t) {
-            float acc = lr[t];
-#pragma unroll
-            for (int r = 0; r < 16; ++r)
-              if (r > t && r < kw) acc = fmaf(-c[r], S.L11[r][t], acc);
-            c[t] = t < kw ? acc : 0.f;
-          }
+          for (int r = 0; r < 16; ++r)
+            if (r >= t && r < kw) acc = fmaf(S.Uinv[j][r], S.Linv[r][t], acc);
+          c[t] = t < kw ? acc : 0.f;
         }
       }
 #pragma unroll
@@ -277,16 +284,17 @@ __global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
         *reinterpret_cast<float4*>(&S.chi[off]) = make_float4(h[0], h[1], h[2], h[3]);
         *reinterpret_cast<float4*>(&S.clo[off]) = make_float4(l[0], l[1], l[2], l[3]);
       }
-      __syncthreads();  // staged pivot rows complete
-      // ---- B operand (K-major): column y = x of the pivot rows, -e_t on the panel columns
+      // ---- B operand (K-major): column y = x of the pivot rows, -e_t on the panel
+      // columns (forward mode: the columns up to the panel's end stay zero)
       {
         const int y = x;
+        const bool zero_col = y >= n || (!GRAD && y < k0 + kw);
         float v[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
           v[t] = t < kw ? S.prow[t][y] : 0.f;
           if (y >= k0 && y < k0 + kw) v[t] = (t < kw && y - k0 == t) ? -1.f : 0.f;
-          if (y >= n) v[t] = 0.f;
+          if (zero_col) v[t] = 0.f;
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -315,31 +323,33 @@ __global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
       }
       umma::fence_proxy_async_smem();
       tc_sync();
-      if (tid == 0) {
-        const uint32_t idesc = umma::idesc_tf32(kTcN, kTcN, true);  // D -= C B^T
+      FX_TOC(tq, 3);
+      if (GRAD || k0 + kw < n) {
+        if (tid == 0) {
+          const uint32_t idesc = umma::idesc_tf32(kTcN, kTcN, true);  // D -= C B^T
 #pragma unroll
-        for (int sl = 0; sl < 2; ++sl) {
-          const uint64_t ah = umma::smem_desc_kmajor(umma::smem_u32(S.chi) + sl * kTcSlab, 128, 256);
-          const uint64_t al = umma::smem_desc_kmajor(umma::smem_u32(S.clo) + sl * kTcSlab, 128, 256);
-          const uint64_t bh = umma::smem_desc_kmajor(umma::smem_u32(S.bhi) + sl * kTcSlab, 128, 256);
-          const uint64_t bm = umma::smem_desc_kmajor(umma::smem_u32(S.bmid) + sl * kTcSlab, 128, 256);
-          const uint64_t bl = umma::smem_desc_kmajor(umma::smem_u32(S.blo) + sl * kTcSlab, 128, 256);
-          umma::mma_tf32(tbase, ah, bh, idesc, true);
-          umma::mma_tf32(tbase, ah, bm, idesc, true);
-          umma::mma_tf32(tbase, ah, bl, idesc, true);
-          umma::mma_tf32(tbase, al, bh, idesc, true);
+          for (int sl = 0; sl < 2; ++sl) {
+            const uint64_t ah = umma::smem_desc_kmajor(umma::smem_u32(S.chi) + sl * kTcSlab, 128, 256);
+            const uint64_t al = umma::smem_desc_kmajor(umma::smem_u32(S.clo) + sl * kTcSlab, 128, 256);
+            const uint64_t bh = umma::smem_desc_kmajor(umma::smem_u32(S.bhi) + sl * kTcSlab, 128, 256);
+            const uint64_t bm = umma::smem_desc_kmajor(umma::smem_u32(S.bmid) + sl * kTcSlab, 128, 256);
+            const uint64_t bl = umma::smem_desc_kmajor(umma::smem_u32(S.blo) + sl * kTcSlab, 128, 256);
+            umma::mma_tf32(tbase, ah, bh, idesc, true);
+            umma::mma_tf32(tbase, ah, bm, idesc, true);
+            umma::mma_tf32(tbase, ah, bl, idesc, true);
+            umma::mma_tf32(tbase, al, bh, idesc, true);
+          }
+          umma::mma_commit(&S.mbar);
         }
-        umma::mma_commit(&S.mbar);
+        __syncwarp();
+        if (!umma::mbar_wait(&S.mbar, phase, kTcWaitIters)) S.bad = 1;
+        phase ^= 1;
+        umma::fence_after_sync();
       }
-      __syncwarp();
-      if (!umma::mbar_wait(&S.mbar, phase, kTcWaitIters)) S.bad = 1;
-      phase ^= 1;
-      umma::fence_after_sync();
-      __syncthreads();  // operand buffers free again
+      FX_TOC(tq, 4);
     }
 
-    // ---- (sign, logabs): pivots in a fixed order (warp 0), permutation parity from the
-    // per-row inversion counts
+    // ---- (sign, logabs): pivots in a fixed order (warp 0) and the permutation parity
     {
       const unsigned pm = __ballot_sync(0xffffffffu, myinv != 0);
       if (lane == 0) S.wpar[warp] = __popc(pm) & 1;
@@ -370,14 +380,14 @@ __global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
         J.sign[b] = S.bad ? __int_as_float(0x7fc00000) : sg;
         J.logabs[b] = S.bad ? __int_as_float(0x7fc00000) : la;
         if (J.value) J.value[b] = sg * expf(la);
-        S.wpar[0] = nz;  // reused below as the singular flag
+        S.nz = nz;
       }
     }
     __syncthreads();
     if (GRAD) {
-      // TMEM[p_s][t] = (A^-1)[s][p_t] = grad[p_t][s]: row x writes column mypos of the
+      // TMEM[p_s][t] = (A^-1)[s][p_t] = grad[p_t][s]: row x writes column pos(x) of the
       // gradient at rows at[t] (each warp store covers one gradient row)
-      const bool zero = S.wpar[0] != 0 || S.bad;
+      const bool zero = S.nz != 0 || S.bad;
       const float f = J.coef ? J.coef[b] : 1.f;
       float* G = J.g + b * (int64_t)n * n;
 #pragma unroll 1
@@ -399,6 +409,7 @@ __global__ void __launch_bounds__(128) lu_tc_kernel(Job<float> J) {
       }
     }
     tc_sync();
+    FX_TOC(tq, 5);
   }
   if (warp == 0) umma::tmem_dealloc(tbase, kTcN);
 }
