@@ -30,11 +30,15 @@ sys.path.insert(0, ROOT)
 METRIC = "slogdet/slogpf matrices/sec fwd & fwd+bwd at 1-8 B200; % of roofline"
 KERNEL = {"slogpf": "pf_fused_kernel", "slogdet": "lu_fused_kernel"}
 SMALL_KERNEL = {"slogpf": "pf_small_kernel", "slogdet": "lu_small_kernel"}
+TC_KERNEL = {"slogpf": "pf_tc_kernel", "slogdet": "lu_tc_kernel"}
 
 
 def kernel_name(a):
-    """The kernel the library dispatches this workload to (register-panel kernels up to
-    n = 256, the one-block-per-matrix generic kernels above)."""
+    """The kernel the library dispatches this workload to: the tensor-memory kernels for
+    float32 / tf32x3 with 8 <= n <= 128 (odd n aside for slogpf), the register-panel
+    kernels up to n = 256, the one-block-per-matrix generic kernels above."""
+    if a.dtype == "f32" and a.prec == "tf32x3" and 8 <= a.n <= 128 and not (a.op == "slogpf" and a.n % 2):
+        return TC_KERNEL[a.op]
     return (SMALL_KERNEL if a.n <= 256 else KERNEL)[a.op]
 
 
