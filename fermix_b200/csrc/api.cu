@@ -146,28 +146,38 @@ int launch_pf_tc(cudaStream_t s, Job<float> J) {
   return FX_OK;
 }
 
-// Tensor-core slogdet (float32, prec tf32x3, 8 <= n <= 128, forward or slogdet gradient):
-// same residency scheme as the Pfaffian kernel above.
+// Tensor-core slogdet (float32, prec tf32x3, 8 <= n <= 256, forward or slogdet gradient):
+// n <= 128 as the Pfaffian kernel above (four 128-thread blocks per SM); 129 <= n <= 256
+// one 256-thread block per SM holding the whole matrix in the SM's 512 TMEM columns, its
+// shared-memory request above half the SM so that no second block (a tcgen05.alloc
+// waiter) is placed beside it.
 constexpr size_t kLuTcSmem = 55 * 1024;  // at most four blocks per SM (4 x 56 KB)
-static_assert(sizeof(LuTcSmem) <= kLuTcSmem, "LuTcSmem too large");
+static_assert(sizeof(LuTcSmemT<128>) <= kLuTcSmem, "LuTcSmem too large");
+constexpr size_t kLuTc256Smem = 120 * 1024;
+static_assert(sizeof(LuTcSmemT<256>) <= kLuTc256Smem, "LuTcSmemT<256> too large");
 
 bool use_lu_tc(int dtype_is_f32, int prec, int n, int mode) {
-  return dtype_is_f32 && prec != FX_PREC_IEEE && n >= 8 && n <= kTcN && (mode == MODE_FWD || mode == MODE_SLOG_GRAD);
+  return dtype_is_f32 && prec != FX_PREC_IEEE && n >= 8 && n <= 2 * kTcN &&
+         (mode == MODE_FWD || mode == MODE_SLOG_GRAD);
 }
 
 int launch_lu_tc(cudaStream_t s, Job<float> J) {
   const DevInfo* D = dev_info();
   if (!D) return FX_ERR_DEVICE;
-  void* k = J.mode == MODE_FWD ? (void*)&lu_tc_kernel<false> : (void*)&lu_tc_kernel<true>;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLuTcSmem) != cudaSuccess)
+  const bool big = J.n > kTcN;
+  void* k = big ? (J.mode == MODE_FWD ? (void*)&lu_tc_kernel<256, false> : (void*)&lu_tc_kernel<256, true>)
+                : (J.mode == MODE_FWD ? (void*)&lu_tc_kernel<128, false> : (void*)&lu_tc_kernel<128, true>);
+  const size_t smem = big ? kLuTc256Smem : kLuTcSmem;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return FX_ERR_CUDA;
   if (cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
     return FX_ERR_CUDA;
-  const int64_t cap = (int64_t)D->sms * 4;
+  const int64_t cap = (int64_t)D->sms * (big ? 1 : 4);
   const int64_t grid = J.B < cap ? J.B : cap;
   if (grid < 1) return FX_OK;
   void* args[] = {&J};
-  if (cudaLaunchKernel(k, dim3((unsigned)grid), dim3(128), args, kLuTcSmem, s) != cudaSuccess) return FX_ERR_CUDA;
+  if (cudaLaunchKernel(k, dim3((unsigned)grid), dim3(big ? 256 : 128), args, smem, s) != cudaSuccess)
+    return FX_ERR_CUDA;
   return FX_OK;
 }
 

@@ -1,4 +1,4 @@
-// Tensor-memory resident Gauss-Jordan LU for float32 slogdet, 8 <= n <= 128,
+// Tensor-memory resident Gauss-Jordan LU for float32 slogdet, 8 <= n <= 256,
 // prec = "tf32x3": forward (sign, logabs) and, in the same pass, A^-1 for the gradient.
 //
 // Reference behaviour: LU with partial pivoting (largest |entry| of the current column
@@ -8,9 +8,11 @@
 // products of src/fermix/_field.py:173-190; gradient A^-T of _lu_parts
 // (src/fermix/_inverse.py:502-531), zero for an exactly singular member.
 //
-// Design (B200). Thread x of the 128-thread block owns row x = TMEM lane x; the matrix
-// stays in TMEM (128 columns) for the whole call and rows are never moved (virtual
-// pivoting). Per panel of 16 columns:
+// Design (B200). Thread x of the NR-thread block owns row x; the matrix stays in TMEM for
+// the whole call and rows are never moved (virtual pivoting). NR = 128: row x = lane x,
+// 128 columns, four blocks per SM. NR = 256 (129 <= n <= 256): the matrix fills the SM's
+// whole TMEM, row x in lane x % 128 at column offset 256 (x / 128), one block per SM and
+// two M = 128, N = 256 MMAs per product. Per panel of 16 columns:
 //   1. every row reads its 16 panel entries into registers and the panel is factored
 //      there: per column a two-instruction warp argmax (redux.sync on a packed |value|
 //      key, then on the row index), ONE block barrier (each warp's candidate row
@@ -36,25 +38,26 @@
 
 namespace fx {
 
-constexpr int kProwLd = kTcN + 4;  // staged pivot rows: 16-byte rows, conflict-free column reads
-
-struct LuTcSmem {
-  float chi[kTcN * 16], clo[kTcN * 16];  // A operand C, K-major, TF32 hi / lo
-  float bhi[kTcN * 16], bmid[kTcN * 16], blo[kTcN * 16];  // B operand, K-major, exact 3-way split
-  uint4 chead[2][4];        // per-warp pivot candidates by step parity: key, row, live ballot
-  float crow[2][4][16];     // the candidates' current panel entries
-  float prow[16][kProwLd];  // the panel's pivot rows (TMEM values)
-  float L11[16][17];        // multipliers of the pivot rows (strict lower part)
-  float U11[16][17];        // the pivot rows' panel entries (upper part)
-  float Linv[16][17];       // L11^-1 (gradient mode)
-  float Uinv[16][17];       // U11^-1 (gradient mode)
-  float dvec[kTcN];         // pivots
-  int at[kTcN];             // pivot position -> row
-  int wpar[4];              // per-warp parity of the inversions
+template <int NR>
+struct LuTcSmemT {
+  static constexpr int NW = NR / 32;
+  float chi[NR * 16], clo[NR * 16];                 // A operand C, K-major, TF32 hi / lo
+  float bhi[NR * 16], bmid[NR * 16], blo[NR * 16];  // B operand, K-major, exact 3-way split
+  uint4 chead[2][NW];                               // per-warp pivot candidates by step parity: key, row, live
+  float crow[2][NW][16];                            // the candidates' current panel entries
+  float prow[16][NR + 4];                           // the panel's pivot rows (16-byte rows, conflict-free columns)
+  float L11[16][17];                                // multipliers of the pivot rows (strict lower part)
+  float U11[16][17];                                // the pivot rows' panel entries (upper part)
+  float Linv[16][17];                               // L11^-1 (gradient mode)
+  float Uinv[16][17];                               // U11^-1 (gradient mode)
+  float dvec[NR];                                   // pivots
+  int at[NR];                                       // pivot position -> row
+  int wpar[NW];                                     // per-warp parity of the inversions
   uint32_t tslot;
   int bad, nz;
   uint64_t mbar;
 };
+using LuTcSmem = LuTcSmemT<128>;
 
 // value == hi + mid + lo exactly, each part a TF32 number (hi, mid round to nearest)
 __device__ __forceinline__ void split3(float v, float& hi, float& mid, float& lo) {
@@ -72,15 +75,18 @@ __device__ __forceinline__ unsigned piv_key(float v, bool live) {
   return __float_as_uint(fabsf(v)) + 2u;
 }
 
-template <bool GRAD>
-__global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
+template <int NR, bool GRAD>
+__global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float> J) {
+  constexpr int NW = NR / 32;
+  constexpr uint32_t kCols = NR == 128 ? 128u : 512u;  // TMEM columns allocated
+  constexpr uint32_t kSlab = NR * 8 * 4;                 // bytes of one K = 8 slab of an NR-row operand
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  LuTcSmem& S = *reinterpret_cast<LuTcSmem*>(smem_raw);
+  LuTcSmemT<NR>& S = *reinterpret_cast<LuTcSmemT<NR>*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = J.n;
-  const int x = tid;  // this thread's row / TMEM lane
+  const int x = tid;  // this thread's row
   if (warp == 0) {
-    umma::tmem_alloc(&S.tslot, kTcN);
+    umma::tmem_alloc(&S.tslot, kCols);
     umma::tmem_relinquish();
   }
   if (tid == 0) {
@@ -89,15 +95,16 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
   }
   tc_sync();
   const uint32_t tbase = S.tslot;
-  const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);
+  // this warp's 32 lanes; rows 128..255 sit 256 columns further right
+  const uint32_t trow = tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(warp >> 2) * 256u;
   uint32_t phase = 0;
 
   for (int64_t b = blockIdx.x; b < J.B; b += gridDim.x) {
     FX_TIC(tq);
     const float* src = J.a + b * (int64_t)n * n;
     if (tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
-    tc_load_matrix(src, n, false, trow, x);
-    int mypos = x < n ? -1 : kTcN;  // pivot position of this row (-1: not yet pivoted)
+    tc_load_matrix<NR>(src, n, false, trow, x);
+    int mypos = x < n ? -1 : NR;  // pivot position of this row (-1: not yet pivoted)
     int myinv = 0;                  // parity of the inversions this row adds as a pivot
     if (tid == 0) S.bad = 0;
     tc_sync();
@@ -137,14 +144,19 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
             for (int q = 0; q < 4; ++q) r4[q] = make_float4(pr[4 * q], pr[4 * q + 1], pr[4 * q + 2], pr[4 * q + 3]);
           }
           __syncthreads();
-          uint4 hd[4];
+          uint4 hd[NW];
 #pragma unroll
-          for (int w = 0; w < 4; ++w) hd[w] = S.chead[s & 1][w];
+          for (int w = 0; w < NW; ++w) hd[w] = S.chead[s & 1][w];
           int pw = 0;
+          unsigned bk = hd[0].x, bp = hd[0].y;
 #pragma unroll
-          for (int w = 1; w < 4; ++w)
-            if (hd[w].x > hd[pw].x || (hd[w].x == hd[pw].x && hd[w].y < hd[pw].y)) pw = w;
-          const int p = (int)(pw == 0 ? hd[0].y : pw == 1 ? hd[1].y : pw == 2 ? hd[2].y : hd[3].y);
+          for (int w = 1; w < NW; ++w)
+            if (hd[w].x > bk || (hd[w].x == bk && hd[w].y < bp)) {
+              pw = w;
+              bk = hd[w].x;
+              bp = hd[w].y;
+            }
+          const int p = (int)bp;
           float ur[16];
           {
             const float4* r4 = reinterpret_cast<const float4*>(S.crow[s & 1][pw]);
@@ -161,10 +173,12 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
           if (x == p) {
             mypos = k0 + s;
             // rows of smaller index still unpivoted: the inversions this pivot adds
-            int cnt = __popc(hd[warp].z & ((1u << lane) - 1u));
+            int cnt = 0;
 #pragma unroll
-            for (int w = 0; w < 4; ++w)
+            for (int w = 0; w < NW; ++w) {
               if (w < warp) cnt += __popc(hd[w].z);
+              if (w == warp) cnt += __popc(hd[w].z & ((1u << lane) - 1u));
+            }
             myinv ^= cnt & 1;
             S.dvec[k0 + s] = piv;
             S.at[k0 + s] = x;
@@ -224,7 +238,7 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
       if (__ballot_sync(0xffffffffu, inP) != 0u) {
         const int tp = mypos - k0;
 #pragma unroll 1
-        for (int c0 = GRAD ? 0 : ((k0 + kw) & ~31); c0 < kTcN; c0 += 32) {
+        for (int c0 = GRAD ? 0 : ((k0 + kw) & ~31); c0 < NR; c0 += 32) {
           uint32_t w[32];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -274,7 +288,7 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint32_t off = umma::kmajor_offset(x, 4 * q, kTcSlab) / 4;
+        const uint32_t off = umma::kmajor_offset(x, 4 * q, kSlab) / 4;
         float h[4], l[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -298,7 +312,7 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint32_t off = umma::kmajor_offset(y, 4 * q, kTcSlab) / 4;
+          const uint32_t off = umma::kmajor_offset(y, 4 * q, kSlab) / 4;
           float h[4], m[4], l[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) split3(v[4 * q + e], h[e], m[e], l[e]);
@@ -326,18 +340,23 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
       FX_TOC(tq, 3);
       if (GRAD || k0 + kw < n) {
         if (tid == 0) {
-          const uint32_t idesc = umma::idesc_tf32(kTcN, kTcN, true);  // D -= C B^T
+          const uint32_t idesc = umma::idesc_tf32(128, NR, true);  // D -= C B^T, M = 128, N = NR
 #pragma unroll
-          for (int sl = 0; sl < 2; ++sl) {
-            const uint64_t ah = umma::smem_desc_kmajor(umma::smem_u32(S.chi) + sl * kTcSlab, 128, 256);
-            const uint64_t al = umma::smem_desc_kmajor(umma::smem_u32(S.clo) + sl * kTcSlab, 128, 256);
-            const uint64_t bh = umma::smem_desc_kmajor(umma::smem_u32(S.bhi) + sl * kTcSlab, 128, 256);
-            const uint64_t bm = umma::smem_desc_kmajor(umma::smem_u32(S.bmid) + sl * kTcSlab, 128, 256);
-            const uint64_t bl = umma::smem_desc_kmajor(umma::smem_u32(S.blo) + sl * kTcSlab, 128, 256);
-            umma::mma_tf32(tbase, ah, bh, idesc, true);
-            umma::mma_tf32(tbase, ah, bm, idesc, true);
-            umma::mma_tf32(tbase, ah, bl, idesc, true);
-            umma::mma_tf32(tbase, al, bh, idesc, true);
+          for (int h = 0; h < NR / 128; ++h) {  // row halves: rows 128 h .. 128 h + 127
+#pragma unroll
+            for (int sl = 0; sl < 2; ++sl) {
+              const uint32_t ao = sl * kSlab + h * 4096u;
+              const uint64_t ah = umma::smem_desc_kmajor(umma::smem_u32(S.chi) + ao, 128, 256);
+              const uint64_t al = umma::smem_desc_kmajor(umma::smem_u32(S.clo) + ao, 128, 256);
+              const uint64_t bh = umma::smem_desc_kmajor(umma::smem_u32(S.bhi) + sl * kSlab, 128, 256);
+              const uint64_t bm = umma::smem_desc_kmajor(umma::smem_u32(S.bmid) + sl * kSlab, 128, 256);
+              const uint64_t bl = umma::smem_desc_kmajor(umma::smem_u32(S.blo) + sl * kSlab, 128, 256);
+              const uint32_t d = tbase + h * 256u;
+              umma::mma_tf32(d, ah, bh, idesc, true);
+              umma::mma_tf32(d, ah, bm, idesc, true);
+              umma::mma_tf32(d, ah, bl, idesc, true);
+              umma::mma_tf32(d, al, bh, idesc, true);
+            }
           }
           umma::mma_commit(&S.mbar);
         }
@@ -354,6 +373,7 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
       const unsigned pm = __ballot_sync(0xffffffffu, myinv != 0);
       if (lane == 0) S.wpar[warp] = __popc(pm) & 1;
     }
+    int par = 0;
     __syncthreads();
     if (warp == 0) {
       float sg = 1.f;
@@ -374,7 +394,8 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
         nz += __shfl_xor_sync(0xffffffffu, nz, off);
       }
       if (lane == 0) {
-        if ((S.wpar[0] ^ S.wpar[1] ^ S.wpar[2] ^ S.wpar[3]) & 1) sg = -sg;
+        for (int w = 0; w < NW; ++w) par ^= S.wpar[w];
+        if (par & 1) sg = -sg;
         if (nz) sg = 0.f;
         const float la = nz ? -INFINITY : lsum;
         J.sign[b] = S.bad ? __int_as_float(0x7fc00000) : sg;
@@ -411,7 +432,7 @@ __global__ void __launch_bounds__(128, 4) lu_tc_kernel(Job<float> J) {
     tc_sync();
     FX_TOC(tq, 5);
   }
-  if (warp == 0) umma::tmem_dealloc(tbase, kTcN);
+  if (warp == 0) umma::tmem_dealloc(tbase, kCols);
 }
 
 }  // namespace fx

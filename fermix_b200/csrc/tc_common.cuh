@@ -35,11 +35,13 @@ __device__ __forceinline__ void tc_prefetch_l2(const float* p, int n) {
 // part as 16-byte loads when every row starts on a 16-byte boundary (scalar otherwise;
 // the 32 rows a warp touches stay in L1 across the column blocks), the transposed part
 // as one coalesced 128-byte load per column (lanes read consecutive entries of a row).
+// NC: TMEM columns to fill (the block's matrix width, 128 or 256).
+template <int NC = kTcN>
 __device__ __forceinline__ void tc_load_matrix(const float* __restrict__ src, int n, bool skew, uint32_t trow,
                                                int x) {
   const bool vec = ((reinterpret_cast<uintptr_t>(src) | ((uintptr_t)n * 4u)) & 15u) == 0;
 #pragma unroll 1
-  for (int c0 = 0; c0 < kTcN; c0 += 32) {
+  for (int c0 = 0; c0 < NC; c0 += 32) {
     float v[32];
 #pragma unroll
     for (int k = 0; k < 32; ++k) v[k] = 0.f;

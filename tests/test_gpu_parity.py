@@ -236,7 +236,7 @@ def test_slogpf_grad(n, dtype):
     assert relerr(g, 0.5 * np.swapaxes(np.linalg.inv(S), -1, -2)) < rel_tol(dtype)
 
 
-@pytest.mark.parametrize("n", [4, 6, 16, 40])
+@pytest.mark.parametrize("n", [4, 6, 16, 40, 130])
 @dtypes
 def test_grad_primal_is_bit_identical_to_forward(n, dtype):
     gen = np.random.default_rng(11)
