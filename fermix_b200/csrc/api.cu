@@ -19,6 +19,7 @@
 #include "small.cuh"
 #include "pf_tc.cuh"
 #include "lu_tc.cuh"
+#include "large_lu.cuh"
 
 namespace {
 
@@ -230,6 +231,105 @@ Job<T> make_job(int64_t batch, int64_t n, const void* a, const void* coef, int c
   return J;
 }
 
+// ---------------------------------------------------------------- large-n LU engine
+// n > kSmallMax, slogdet forward and gradient: the panel loop of large_lu.cuh over slices
+// of the batch. Workspace per matrix: the matrix itself, the panel coefficients and
+// pivot-row snapshot, L11 / U11, pivots and index arrays; each array 256-byte aligned.
+constexpr int kLgSliceBlocks = 4;  // a slice holds at most SMs x 4 matrices
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+template <typename T>
+struct LgLayout {
+  size_t M, C, P, LU, piv, ipiv, cand, perm, flag, total;
+  LgLayout(int64_t bs, int n) {
+    constexpr int NB = LgCfg<T>::NB;
+    const int nchunk = (n + kLgChunk - 1) / kLgChunk;
+    size_t o = 0;
+    M = o;    o = align256(o + (size_t)bs * n * n * sizeof(T));
+    C = o;    o = align256(o + (size_t)bs * n * NB * sizeof(T));
+    P = o;    o = align256(o + (size_t)bs * NB * n * sizeof(T));
+    LU = o;   o = align256(o + (size_t)bs * 2 * NB * NB * sizeof(T));
+    piv = o;  o = align256(o + (size_t)bs * n * sizeof(T));
+    ipiv = o; o = align256(o + (size_t)bs * n * sizeof(int));
+    cand = o; o = align256(o + (size_t)bs * nchunk * NB * sizeof(int));
+    perm = o; o = align256(o + (size_t)bs * n * sizeof(int));
+    flag = o; o = align256(o + (size_t)bs * sizeof(int));
+    total = o;
+  }
+};
+
+template <typename T>
+int64_t lg_slice(int64_t batch) {
+  const DevInfo* D = dev_info();
+  const int64_t cap = (int64_t)(D ? D->sms : 148) * kLgSliceBlocks;
+  return batch < cap ? batch : cap;
+}
+
+template <typename T>
+size_t lg_ws_bytes(int64_t batch, int n) {
+  return LgLayout<T>(lg_slice<T>(batch), n).total;
+}
+
+template <typename T>
+int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad) {
+  constexpr int NB = LgCfg<T>::NB;
+  const int n = J.n;
+  if (!ws) return FX_ERR_WORKSPACE;
+  int64_t bs = lg_slice<T>(J.B);
+  while (bs > 1 && LgLayout<T>(bs, n).total > wsb) bs = bs / 2;
+  const LgLayout<T> Lw(bs, n);
+  if (Lw.total > wsb) return FX_ERR_WORKSPACE;
+  unsigned char* w = static_cast<unsigned char*>(ws);
+  LgArgs<T> A{};
+  A.M = reinterpret_cast<T*>(w + Lw.M);
+  A.C = reinterpret_cast<T*>(w + Lw.C);
+  A.P = reinterpret_cast<T*>(w + Lw.P);
+  A.LU11 = reinterpret_cast<T*>(w + Lw.LU);
+  A.piv = reinterpret_cast<T*>(w + Lw.piv);
+  A.ipiv = reinterpret_cast<int*>(w + Lw.ipiv);
+  A.cand = reinterpret_cast<int*>(w + Lw.cand);
+  A.perm = reinterpret_cast<int*>(w + Lw.perm);
+  A.flag = reinterpret_cast<int*>(w + Lw.flag);
+  A.n = n;
+  const size_t leaf_smem = kLgChunk * sizeof(int) + lg_gepp_smem<T>();
+  const size_t tree_smem = lg_tree_smem<T>((n + kLgChunk - 1) / kLgChunk);
+  void* tree_k = (void*)&lg_tree_kernel<T>;
+  if (tree_smem > 48 * 1024 &&
+      cudaFuncSetAttribute(tree_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tree_smem) != cudaSuccess)
+    return FX_ERR_CUDA;
+  for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
+    const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);
+    if (cudaMemcpyAsync(A.M, J.a + b0 * (int64_t)n * n, (size_t)cnt * n * n * sizeof(T), cudaMemcpyDeviceToDevice,
+                        s) != cudaSuccess)
+      return FX_ERR_CUDA;
+    for (int k0 = 0; k0 < n; k0 += NB) {
+      A.k0 = k0;
+      A.kw = n - k0 < NB ? n - k0 : NB;
+      A.nchunk = (n - k0 + kLgChunk - 1) / kLgChunk;
+      lg_leaf_kernel<T><<<dim3(A.nchunk, cnt), kLgChunk, leaf_smem, s>>>(A);
+      lg_tree_kernel<T><<<cnt, kLgChunk, tree_smem, s>>>(A);
+      const int c_lo = grad ? 0 : k0;
+      lg_swap_kernel<T><<<dim3((n - c_lo + 255) / 256, cnt), 256, 0, s>>>(A, c_lo);
+      const int r_lo = grad ? 0 : k0;
+      if (grad) {
+        lg_coef_kernel<T, true><<<dim3((n - r_lo + 255) / 256, cnt), 256, 0, s>>>(A, r_lo);
+      } else {
+        lg_coef_kernel<T, false><<<dim3((n - r_lo + 255) / 256, cnt), 256, 0, s>>>(A, r_lo);
+      }
+      const int u_lo = grad ? 0 : k0 + A.kw;
+      if (u_lo < n) lg_update_kernel<T><<<dim3((n - u_lo + 63) / 64, (n - u_lo + 63) / 64, cnt), 256, 0, s>>>(A, u_lo, u_lo);
+    }
+    lg_finish_kernel<T><<<cnt, 32, 0, s>>>(A, J, b0, grad ? 1 : 0);
+    if (grad) {
+      lg_check_kernel<T><<<dim3(16, cnt), 256, 0, s>>>(A);
+      lg_grad_kernel<T><<<dim3((n + 31) / 32, (n + 31) / 32, cnt), 256, 0, s>>>(A, J, b0);
+    }
+    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  }
+  return FX_OK;
+}
+
 template <typename T>
 int run_det(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* a, const void* coef, int conj_out,
             int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb) {
@@ -247,6 +347,17 @@ int run_det(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* a, c
       F.g = nullptr;
       return launch_lu_tc(s, F);
     }
+  }
+  if (n > kSmallMax) {
+    if (mode == MODE_FWD || mode == MODE_SLOG_GRAD) return run_large_lu<T>(s, J, ws, wsb, mode == MODE_SLOG_GRAD);
+    // the det adjugate comes from the generic kernel; (sign, logabs, value) are rewritten
+    // by the large-n forward (same stream, same workspace) to equal fermix_slogdet's bits
+    int e = launch_fused<T, false>(s, J, ws, wsb);
+    if (e) return e;
+    Job<T> F = J;
+    F.mode = MODE_FWD;
+    F.g = nullptr;
+    return run_large_lu<T>(s, F, ws, wsb, false);
   }
   return launch_fused<T, false>(s, J, ws, wsb);
 }
@@ -304,8 +415,13 @@ size_t ws_bytes_t(int op, int64_t batch, int64_t n, int grad) {
   if (op == FX_OP_SLOGPF && std::is_same<T, float>::value && n <= kTcN) return 0;  // TMEM / shared memory only
   Plan P;
   int e = op == FX_OP_SLOGPF ? plan_fused<T, true>(batch, (int)n, mode, P) : plan_fused<T, false>(batch, (int)n, mode, P);
-  if (e || P.in_smem) return 0;
-  return (size_t)P.grid * P.slot;
+  const size_t generic = (e || P.in_smem) ? 0 : (size_t)P.grid * P.slot;
+  if (op == FX_OP_SLOGDET && n > kSmallMax) {
+    // the large-n engine (the det adjugate also runs the generic kernel first)
+    const size_t lg = lg_ws_bytes<T>(batch, (int)n);
+    return lg > generic ? lg : generic;
+  }
+  return generic;
 }
 
 }  // namespace

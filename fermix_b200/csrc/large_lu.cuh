@@ -1,0 +1,472 @@
+// Blocked LU / Gauss-Jordan engine for slogdet and its gradient at n > 256, every dtype:
+// a host-driven loop over panels of NB columns, each panel a short sequence of batched
+// kernels (grid = the batch slice x tiles), the matrices in the caller's workspace.
+//
+// Reference behaviour: the blocked LU of src/fermix/_lu.py:51-120 (panel) and :153-217
+// (trailing update) with sign / log|det| as in :543-611 (pivot = largest abs1 entry of
+// the column, first occurrence; a zero pivot gives a zero multiplier column, sign 0 and
+// logabs -inf); gradient A^-T (src/fermix/_inverse.py:502-531), zero for an exactly
+// singular or non-finite member.
+//
+// Per panel K = [k0, k0 + kw):
+//   1. pivots by tall-skinny LU: every chunk of 512 rows runs partial pivoting on its
+//      panel rows in registers (lg_leaf_kernel); the chunks' pivot rows then compete in
+//      one more partial-pivoting pass that also yields L11 / U11 (lg_tree_kernel). With a
+//      single chunk (n - k0 <= 512) this IS partial pivoting; above, the pivot order is
+//      the tournament's (a documented deviation, same determinant);
+//   2. the row interchanges on the whole rows, and a snapshot Pb of the pivot rows
+//      (lg_swap_kernel);
+//   3. per row, the coefficients C_x = l_x L11^-1 with l_x = M_xK U11^-1 -- forward then
+//      back substitution, the same sequential FMA chains as the elimination, so that a
+//      row duplicating pivot row s gets exactly e_s (lg_coef_kernel);
+//   4. M -= C Pb over the trailing block (forward) or the whole matrix outside K
+//      (gradient), one FMA chain per entry in panel-column order (lg_update_kernel).
+// Gradient mode is the Gauss-Jordan exchange: pivot rows take C = e_j + (A_PK^-1)_j,
+// rows above the panel take their C as well, and the panel columns are replaced by C
+// (and A_PK^-1 for the pivot rows). After the last panel the workspace holds
+// (P A)^-1 = A^-1 P^T; lg_grad_kernel writes grad[perm[k]][j] = M[j][k].
+#pragma once
+#include "fused_lu.cuh"
+
+namespace fx {
+
+constexpr int kLgChunk = 512;  // rows per tall-skinny leaf (one thread per row)
+
+template <typename T>
+struct LgCfg {
+  static constexpr int NB = sizeof(T) <= 8 ? 32 : 16;  // panel width (registers per row)
+};
+
+// Per-matrix state of the engine, all in the workspace (bs = matrices in the slice).
+template <typename T>
+struct LgArgs {
+  T* M;          // bs x n x n, the matrices being factorised (row-major)
+  T* C;          // bs x n x NB coefficients of the current panel
+  T* P;          // bs x NB x n snapshot of the current pivot rows
+  T* LU11;       // bs x 2 x NB x NB: L11 (strict lower), U11 (upper)
+  T* piv;        // bs x n pivots
+  int* ipiv;     // bs x n interchanges (LAPACK order: row k swapped with ipiv[k])
+  int* cand;     // bs x nchunk x NB leaf pivot rows
+  int* perm;     // bs x n row permutation (gradient)
+  int* flag;     // bs: non-finite entry seen in the inverse (gradient)
+  int n, k0, kw, nchunk;
+};
+
+template <typename T>
+__device__ __forceinline__ typename Sc<T>::R lg_key(T v, bool live) {
+  typedef typename Sc<T>::R R;
+  if (!live) return R(-1);
+  const R a = abs1(v);
+  return a != a ? R(-0.5) : a;  // NaN: a candidate only when every candidate is NaN
+}
+
+// Partial pivoting on the panel columns [k0, k0 + kw) of up to 512 listed rows (thread i
+// holds row rows[i] in registers). Writes the kw pivot rows in order to out[]; with
+// want_lu also L11 / U11 and the pivots. Every block thread must call it.
+template <typename T, int NB>
+__device__ void lg_gepp(const T* __restrict__ Mb, int n, int k0, int kw, const int* rows, int count, int* out,
+                        T* L11, T* U11, T* pivs, bool want_lu, unsigned char* smem) {
+  typedef typename Sc<T>::R R;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  constexpr int NW = kLgChunk / 32;
+  R* skey = reinterpret_cast<R*>(smem);                         // [2][NW]
+  int* spos = reinterpret_cast<int*>(skey + 2 * NW);            // [2][NW] row position
+  int* sidx = spos + 2 * NW;                                    // [2][NW] list index
+  T* srow = reinterpret_cast<T*>(sidx + 2 * NW + (2 * NW) % 4);  // [2][NW][NB]
+  const bool have = tid < count;
+  const int myrow = have ? rows[tid] : 0x7fffffff;
+  T pr[NB];
+#pragma unroll
+  for (int t = 0; t < NB; ++t) pr[t] = (have && t < kw) ? Mb[(size_t)myrow * n + k0 + t] : s_zero<T>();
+  int mystep = have ? -1 : NB;
+#pragma unroll
+  for (int s = 0; s < NB; ++s) {
+    if (s < kw) {
+      const bool live = mystep < 0;
+      R bv = lg_key(pr[s], live);
+      int bp = live ? myrow : 0x7fffffff;
+      int bi = tid;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const R ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int op = __shfl_xor_sync(0xffffffffu, bp, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && op < bp)) {
+          bv = ov;
+          bp = op;
+          bi = oi;
+        }
+      }
+      const int par = s & 1;
+      if (tid == bi) {
+        skey[par * NW + warp] = bv;
+        spos[par * NW + warp] = bp;
+        sidx[par * NW + warp] = bi;
+#pragma unroll
+        for (int t = 0; t < NB; ++t) srow[(par * NW + warp) * NB + t] = pr[t];
+      }
+      __syncthreads();
+      int w0 = 0;
+      R kv = skey[par * NW];
+      int kp = spos[par * NW];
+      for (int w = 1; w < NW; ++w) {
+        const R ov = skey[par * NW + w];
+        const int op = spos[par * NW + w];
+        if (ov > kv || (ov == kv && op < kp)) {
+          kv = ov;
+          kp = op;
+          w0 = w;
+        }
+      }
+      const bool valid = kp != 0x7fffffff;  // false once fewer rows than steps remain
+      const int wi = sidx[par * NW + w0];
+      const T* u = srow + (par * NW + w0) * NB;
+      const T pv = u[s];
+      if (valid && tid == wi) {
+        mystep = s;
+      } else if (valid && mystep < 0) {
+        const T l = is_zero(pv) ? s_zero<T>() : sdiv(pr[s], pv);
+        pr[s] = l;
+#pragma unroll
+        for (int t = 0; t < NB; ++t)
+          if (t > s) pr[t] = fms(pr[t], l, u[t]);
+      }
+      if (tid == 0) {
+        out[s] = valid ? kp : -1;
+        if (want_lu) pivs[s] = pv;
+      }
+    }
+  }
+  if (want_lu && mystep >= 0 && mystep < kw) {
+    const int j = mystep;
+#pragma unroll
+    for (int t = 0; t < NB; ++t) {
+      if (t < j) L11[j * NB + t] = pr[t];
+      else U11[j * NB + t] = pr[t];
+    }
+  }
+  __syncthreads();
+}
+
+template <typename T>
+constexpr size_t lg_gepp_smem() {
+  typedef typename Sc<T>::R R;
+  constexpr int NW = kLgChunk / 32;
+  return 2 * NW * sizeof(R) + 4 * NW * sizeof(int) + 64 + 2 * NW * LgCfg<T>::NB * sizeof(T) + 64;
+}
+
+// 1. leaf: chunk blockIdx.x of the rows [k0, n) of matrix blockIdx.y
+template <typename T>
+__global__ void __launch_bounds__(kLgChunk) lg_leaf_kernel(LgArgs<T> A) {
+  constexpr int NB = LgCfg<T>::NB;
+  extern __shared__ __align__(16) unsigned char smem[];
+  int* rows = reinterpret_cast<int*>(smem);
+  const int b = blockIdx.y, c = blockIdx.x, n = A.n;
+  const int r0 = A.k0 + c * kLgChunk;
+  const int count = min(kLgChunk, n - r0);
+  rows[threadIdx.x] = r0 + threadIdx.x;
+  __syncthreads();
+  lg_gepp<T, NB>(A.M + (size_t)b * n * n, n, A.k0, A.kw, rows, count, A.cand + ((size_t)b * A.nchunk + c) * NB,
+                 nullptr, nullptr, nullptr, false, smem + kLgChunk * sizeof(int));
+}
+
+// 2. tree: partial pivoting over the leaves' candidates (in chunk order, at most 512 rows
+// per pass: winners of a pass compete again with the next candidates) gives the panel's
+// pivot rows, L11, U11 and the pivots; thread 0 turns the rows into LAPACK-order
+// interchanges.
+template <typename T>
+__global__ void __launch_bounds__(kLgChunk) lg_tree_kernel(LgArgs<T> A) {
+  constexpr int NB = LgCfg<T>::NB;
+  extern __shared__ __align__(16) unsigned char smem[];
+  int* rows = reinterpret_cast<int*>(smem);  // [512] current pass
+  int* sel = rows + kLgChunk;                // [NB] winners
+  int* allc = sel + NB;                      // [nchunk * NB] compacted candidates
+  int* ntot = allc + A.nchunk * NB;          // [1]
+  unsigned char* scratch = smem + (size_t)(kLgChunk + NB + A.nchunk * NB + 4) * sizeof(int);
+  const int b = blockIdx.x, n = A.n, kw = A.kw, k0 = A.k0;
+  const int* cb = A.cand + (size_t)b * A.nchunk * NB;
+  if (threadIdx.x == 0) {
+    int m = 0;
+    for (int i = 0; i < A.nchunk * kw; ++i) {
+      const int r = cb[(i / kw) * NB + i % kw];
+      if (r >= 0) allc[m++] = r;
+    }
+    *ntot = m;
+  }
+  __syncthreads();
+  const int total = *ntot;
+  int count = min(total, kLgChunk);
+  for (int i = threadIdx.x; i < count; i += blockDim.x) rows[i] = allc[i];
+  int consumed = count;
+  const T* Mb = A.M + (size_t)b * n * n;
+  while (consumed < total) {
+    __syncthreads();
+    lg_gepp<T, NB>(Mb, n, k0, kw, rows, count, sel, nullptr, nullptr, nullptr, false, scratch);
+    const int more = min(total - consumed, kLgChunk - kw);
+    if (threadIdx.x < kw) rows[threadIdx.x] = sel[threadIdx.x];
+    for (int i = threadIdx.x; i < more; i += blockDim.x) rows[kw + i] = allc[consumed + i];
+    count = kw + more;
+    consumed += more;
+  }
+  __syncthreads();
+  T* LU = A.LU11 + (size_t)b * 2 * NB * NB;
+  lg_gepp<T, NB>(Mb, n, k0, kw, rows, count, sel, LU, LU + NB * NB, A.piv + (size_t)b * n + k0, true, scratch);
+  if (threadIdx.x == 0) {
+    // positions of the chosen rows as earlier interchanges move them
+    int cur[NB];
+    for (int j = 0; j < kw; ++j) cur[j] = sel[j];
+    int* ip = A.ipiv + (size_t)b * n;
+    for (int j = 0; j < kw; ++j) {
+      const int t = cur[j];
+      ip[k0 + j] = t;
+      for (int q = j + 1; q < kw; ++q)
+        if (cur[q] == k0 + j) cur[q] = t;
+    }
+  }
+}
+
+template <typename T>
+inline size_t lg_tree_smem(int nchunk) {
+  return (size_t)(kLgChunk + LgCfg<T>::NB + nchunk * LgCfg<T>::NB + 4) * sizeof(int) + lg_gepp_smem<T>();
+}
+
+// 3. interchanges on the columns [c_lo, n) of the whole rows, then the pivot-row snapshot
+template <typename T>
+__global__ void __launch_bounds__(256) lg_swap_kernel(LgArgs<T> A, int c_lo) {
+  constexpr int NB = LgCfg<T>::NB;
+  const int b = blockIdx.y, n = A.n, k0 = A.k0, kw = A.kw;
+  const int c = c_lo + blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n) return;
+  T* Mb = A.M + (size_t)b * n * n;
+  const int* ip = A.ipiv + (size_t)b * n;
+  for (int j = 0; j < kw; ++j) {
+    const int p = ip[k0 + j];
+    if (p != k0 + j) {
+      const T x = Mb[(size_t)(k0 + j) * n + c];
+      Mb[(size_t)(k0 + j) * n + c] = Mb[(size_t)p * n + c];
+      Mb[(size_t)p * n + c] = x;
+    }
+  }
+  T* Pb = A.P + (size_t)b * NB * n;
+  for (int j = 0; j < kw; ++j) Pb[(size_t)j * n + c] = Mb[(size_t)(k0 + j) * n + c];
+}
+
+// 4. coefficients of rows [r_lo, n) (one thread per row)
+template <typename T, bool GRAD>
+__global__ void __launch_bounds__(256) lg_coef_kernel(LgArgs<T> A, int r_lo) {
+  constexpr int NB = LgCfg<T>::NB;
+  __shared__ T sL[NB * NB], sU[NB * NB];
+  const int b = blockIdx.y, n = A.n, k0 = A.k0, kw = A.kw;
+  const T* LU = A.LU11 + (size_t)b * 2 * NB * NB;
+  for (int i = threadIdx.x; i < NB * NB; i += blockDim.x) {
+    sL[i] = LU[i];
+    sU[i] = LU[NB * NB + i];
+  }
+  __syncthreads();
+  const int r = r_lo + blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  T* Mb = A.M + (size_t)b * n * n;
+  T* row = Mb + (size_t)r * n + k0;
+  T c[NB];
+  if (r >= k0 && r < k0 + kw) {
+    if (!GRAD) return;
+    // pivot row j: w = e_j U11^-1, then c = w L11^-1 (row j of A_PK^-1)
+    const int j = r - k0;
+    T w[NB];
+#pragma unroll
+    for (int t = 0; t < NB; ++t) {
+      T acc = (t == j) ? s_one<T>() : s_zero<T>();
+#pragma unroll
+      for (int q = 0; q < NB; ++q)
+        if (q < t) acc = fms(acc, w[q], sU[q * NB + t]);
+      const T d = sU[t * NB + t];
+      w[t] = (t < kw && t >= j && !is_zero(d)) ? sdiv(acc, d) : s_zero<T>();
+    }
+#pragma unroll
+    for (int t = NB - 1; t >= 0; --t) {
+      T acc = w[t];
+#pragma unroll
+      for (int q = 0; q < NB; ++q)
+        if (q > t && q < kw) acc = fms(acc, c[q], sL[q * NB + t]);
+      c[t] = t < kw ? acc : s_zero<T>();
+    }
+#pragma unroll
+    for (int t = 0; t < NB; ++t)
+      if (t < kw) row[t] = c[t];  // the exchanged block: A_PK^-1
+#pragma unroll
+    for (int t = 0; t < NB; ++t)
+      if (t == j) c[t] = add(c[t], s_one<T>());
+  } else {
+    // l = M_xK U11^-1 (the elimination's FMA chains), then C L11 = l
+    T l[NB];
+#pragma unroll
+    for (int t = 0; t < NB; ++t) {
+      T acc = t < kw ? row[t] : s_zero<T>();
+#pragma unroll
+      for (int q = 0; q < NB; ++q)
+        if (q < t) acc = fms(acc, l[q], sU[q * NB + t]);
+      const T d = sU[t * NB + t];
+      l[t] = (t < kw && !is_zero(d)) ? sdiv(acc, d) : s_zero<T>();
+    }
+#pragma unroll
+    for (int t = NB - 1; t >= 0; --t) {
+      T acc = l[t];
+#pragma unroll
+      for (int q = 0; q < NB; ++q)
+        if (q > t && q < kw) acc = fms(acc, c[q], sL[q * NB + t]);
+      c[t] = t < kw ? acc : s_zero<T>();
+    }
+    if (GRAD) {
+#pragma unroll
+      for (int t = 0; t < NB; ++t)
+        if (t < kw) row[t] = c[t];
+    }
+  }
+  T* cr = A.C + ((size_t)b * n + r) * NB;
+#pragma unroll
+  for (int t = 0; t < NB; ++t) cr[t] = c[t];
+}
+
+// 5. M[x][y] -= sum_s C[x][s] P[s][y] over rows [r_lo, n) x columns [c_lo, n) minus the
+// panel columns; 64 x 64 tiles, 256 threads, 4 x 4 entries per thread, one FMA chain per
+// entry in panel-column order.
+template <typename T>
+__global__ void __launch_bounds__(256) lg_update_kernel(LgArgs<T> A, int r_lo, int c_lo) {
+  constexpr int NB = LgCfg<T>::NB;
+  constexpr int TM = 64, TN = 64;
+  __shared__ T sC[TM][NB + 1];
+  __shared__ T sP[NB][TN];
+  const int b = blockIdx.z, n = A.n, k0 = A.k0, kw = A.kw;
+  const int r0 = r_lo + blockIdx.y * TM, c0 = c_lo + blockIdx.x * TN;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  T* Mb = A.M + (size_t)b * n * n;
+  const T* Cb = A.C + (size_t)b * n * NB;
+  const T* Pb = A.P + (size_t)b * NB * n;
+  for (int i = tid; i < TM * NB; i += 256) {
+    const int rr = i / NB, s = i % NB, r = r0 + rr;
+    sC[rr][s] = (r < n && s < kw) ? Cb[(size_t)r * NB + s] : s_zero<T>();
+  }
+  for (int i = tid; i < NB * TN; i += 256) {
+    const int s = i / TN, cc = i % TN, c = c0 + cc;
+    sP[s][cc] = (c < n && s < kw) ? Pb[(size_t)s * n + c] : s_zero<T>();
+  }
+  __syncthreads();
+  int rr[4], cc[4];
+  bool rv[4], cv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    rr[i] = r0 + ty + 16 * i;
+    rv[i] = rr[i] < n;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    cc[j] = c0 + tx + 16 * j;
+    cv[j] = cc[j] < n && (cc[j] < k0 || cc[j] >= k0 + kw);
+  }
+  T acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = (rv[i] && cv[j]) ? Mb[(size_t)rr[i] * n + cc[j]] : s_zero<T>();
+  for (int s = 0; s < kw; ++s) {
+    T a[4], p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = sC[ty + 16 * i][s];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) p[j] = sP[s][tx + 16 * j];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = fms(acc[i][j], a[i], p[j]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (rv[i] && cv[j]) Mb[(size_t)rr[i] * n + cc[j]] = acc[i][j];
+}
+
+// 6. (sign, logabs) from the pivots and interchanges; gradient mode also the row
+// permutation for the output (one warp per matrix)
+template <typename T>
+__global__ void __launch_bounds__(32) lg_finish_kernel(LgArgs<T> A, Job<T> J, int64_t b0, int grad) {
+  typedef typename Sc<T>::R R;
+  const int b = blockIdx.x, n = A.n, lane = threadIdx.x;
+  const T* pv = A.piv + (size_t)b * n;
+  const int* ip = A.ipiv + (size_t)b * n;
+  if (lane == 0) {
+    T sgn = s_one<T>();
+    KSum<R> ls;
+    ls.init();
+    int par = 0, nz = 0;
+    for (int k = 0; k < n; ++k) {
+      const T d = pv[k];
+      par ^= ip[k] != k;
+      sgn = mul(sgn, unit(d));
+      ls.add(rlog(mag(d)));
+      nz += is_zero(d);
+    }
+    if (par) sgn = neg(sgn);
+    if (nz) sgn = s_zero<T>();
+    if constexpr (Sc<T>::cx) {
+      R m = rhypot(sgn.re, sgn.im);
+      if (m != R(0)) sgn = {rdiv(sgn.re, m), rdiv(sgn.im, m)};
+    }
+    const R la = nz ? -INFINITY : ls.value();
+    J.sign[b0 + b] = sgn;
+    J.logabs[b0 + b] = la;
+    if (J.value) J.value[b0 + b] = scale(sgn, rexp(la));
+    A.flag[b] = nz ? 1 : 0;
+    if (grad) {
+      int* pm = A.perm + (size_t)b * n;
+      for (int k = 0; k < n; ++k) pm[k] = k;
+      for (int k = 0; k < n; ++k) {
+        const int p = ip[k];
+        const int x = pm[k];
+        pm[k] = pm[p];
+        pm[p] = x;
+      }
+    }
+  }
+}
+
+// 7. non-finite entries of the inverse (gradient mode): flag the matrix
+template <typename T>
+__global__ void __launch_bounds__(256) lg_check_kernel(LgArgs<T> A) {
+  const int b = blockIdx.y, n = A.n;
+  const size_t nn = (size_t)n * n;
+  const T* Mb = A.M + (size_t)b * nn;
+  bool bad = false;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nn; i += (size_t)gridDim.x * blockDim.x)
+    bad |= !is_finite(Mb[i]);
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(A.flag + b, 2);
+}
+
+// 8. grad[perm[k]][j] = f * M[j][k] (f = coef, conjugated on request; zero when flagged),
+// through a 32 x 32 shared-memory transpose
+template <typename T>
+__global__ void __launch_bounds__(256) lg_grad_kernel(LgArgs<T> A, Job<T> J, int64_t b0) {
+  __shared__ T tile[32][33];
+  const int b = blockIdx.z, n = A.n;
+  const int j0 = blockIdx.y * 32, k0 = blockIdx.x * 32;
+  const T* Mb = A.M + (size_t)b * n * n;
+  const int* pm = A.perm + (size_t)b * n;
+  const bool zero = A.flag[b] != 0;
+  const T f = J.coef ? J.coef[b0 + b] : s_one<T>();
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int jj = ty; jj < 32; jj += 8) {
+    const int j = j0 + jj, k = k0 + tx;
+    tile[jj][tx] = (j < n && k < n) ? Mb[(size_t)j * n + k] : s_zero<T>();
+  }
+  __syncthreads();
+  T* G = J.g + (size_t)(b0 + b) * n * n;
+  for (int kk = ty; kk < 32; kk += 8) {
+    const int k = k0 + kk, j = j0 + tx;
+    if (k < n && j < n) {
+      T v = zero ? s_zero<T>() : mul(f, tile[tx][kk]);
+      G[(size_t)pm[k] * n + j] = maybe_conj(J, v);
+    }
+  }
+}
+
+}  // namespace fx
