@@ -271,8 +271,10 @@ size_t lg_ws_bytes(int64_t batch, int n) {
   return LgLayout<T>(lg_slice<T>(batch), n).total;
 }
 
+// primal: write (sign, logabs, value); pf_grad: the input is skew-symmetrised when J.skew,
+// the gradient is S^-T / 2 and zero where J.sign (the Pfaffian forward's) is zero.
 template <typename T>
-int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad) {
+int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool pf_grad = false) {
   constexpr int NB = LgCfg<T>::NB;
   const int n = J.n;
   if (!ws) return FX_ERR_WORKSPACE;
@@ -292,6 +294,9 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad) {
   A.perm = reinterpret_cast<int*>(w + Lw.perm);
   A.flag = reinterpret_cast<int*>(w + Lw.flag);
   A.n = n;
+  A.primal = pf_grad ? 0 : 1;
+  A.gscale = pf_grad ? typename Sc<T>::R(0.5) : typename Sc<T>::R(1);
+  A.zsign = pf_grad ? J.sign : nullptr;
   const size_t leaf_smem = kLgChunk * sizeof(int) + lg_gepp_smem<T>();
   const size_t tree_smem = lg_tree_smem<T>((n + kLgChunk - 1) / kLgChunk);
   void* tree_k = (void*)&lg_tree_kernel<T>;
@@ -300,9 +305,12 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad) {
     return FX_ERR_CUDA;
   for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
     const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);
-    if (cudaMemcpyAsync(A.M, J.a + b0 * (int64_t)n * n, (size_t)cnt * n * n * sizeof(T), cudaMemcpyDeviceToDevice,
-                        s) != cudaSuccess)
+    if (pf_grad && J.skew) {
+      lg_skew_copy_kernel<T><<<dim3((n + 31) / 32, (n + 31) / 32, cnt), 256, 0, s>>>(A.M, J.a + b0 * (int64_t)n * n, n);
+    } else if (cudaMemcpyAsync(A.M, J.a + b0 * (int64_t)n * n, (size_t)cnt * n * n * sizeof(T),
+                               cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
       return FX_ERR_CUDA;
+    }
     for (int k0 = 0; k0 < n; k0 += NB) {
       A.k0 = k0;
       A.kw = n - k0 < NB ? n - k0 : NB;
@@ -389,6 +397,16 @@ int run_pf(cudaStream_t s, int prec, int64_t batch, int64_t n, int skew, const v
       return launch_pf_tc(s, F);
     }
   }
+  if (n > kSmallMax && mode == MODE_SLOG_GRAD) {
+    // the Parlett-Reid forward gives (sign, logabs, value); the gradient S^-T / 2 comes
+    // from the large-n Gauss-Jordan engine (same stream, the workspace reused)
+    Job<T> F = J;
+    F.mode = MODE_FWD;
+    F.g = nullptr;
+    int e = launch_fused<T, true>(s, F, ws, wsb);
+    if (e) return e;
+    return run_large_lu<T>(s, J, ws, wsb, true, true);
+  }
   return launch_fused<T, true>(s, J, ws, wsb);
 }
 
@@ -416,10 +434,16 @@ size_t ws_bytes_t(int op, int64_t batch, int64_t n, int grad) {
   Plan P;
   int e = op == FX_OP_SLOGPF ? plan_fused<T, true>(batch, (int)n, mode, P) : plan_fused<T, false>(batch, (int)n, mode, P);
   const size_t generic = (e || P.in_smem) ? 0 : (size_t)P.grid * P.slot;
-  if (op == FX_OP_SLOGDET && n > kSmallMax) {
-    // the large-n engine (the det adjugate also runs the generic kernel first)
+  if (n > kSmallMax && (op == FX_OP_SLOGDET || grad)) {
+    // the large-n engine (the det adjugate and the Pfaffian gradient also run the generic
+    // kernel, one after the other on the same workspace)
     const size_t lg = lg_ws_bytes<T>(batch, (int)n);
-    return lg > generic ? lg : generic;
+    Plan F;
+    const size_t fwd = (op == FX_OP_SLOGPF && plan_fused<T, true>(batch, (int)n, MODE_FWD, F) == FX_OK && !F.in_smem)
+                           ? (size_t)F.grid * F.slot
+                           : 0;
+    size_t m = lg > generic ? lg : generic;
+    return m > fwd ? m : fwd;
   }
   return generic;
 }

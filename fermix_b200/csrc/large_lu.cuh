@@ -50,7 +50,35 @@ struct LgArgs {
   int* perm;     // bs x n row permutation (gradient)
   int* flag;     // bs: non-finite entry seen in the inverse (gradient)
   int n, k0, kw, nchunk;
+  // caller options: write (sign, logabs, value) (slogdet) or not (the Pfaffian gradient,
+  // whose primal comes from the Parlett-Reid forward); scale of the gradient (1 for
+  // slogdet, 1/2 for slogpf: d log pf / dS = S^-T / 2); zsign: a zero entry zeroes that
+  // member's gradient (the Pfaffian forward's exact singularity)
+  int primal;
+  typename Sc<T>::R gscale;
+  const T* zsign;
 };
+
+// M = (a - a^T) / 2 of matrix blockIdx.z (32 x 32 tiles through shared memory)
+template <typename T>
+__global__ void __launch_bounds__(256) lg_skew_copy_kernel(T* M, const T* a, int n) {
+  __shared__ T tile[32][33];
+  typedef typename Sc<T>::R R;
+  const int b = blockIdx.z, i0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const T* ab = a + (size_t)b * n * n;
+  // tile of a^T: rows j0.., columns i0..
+  for (int r = ty; r < 32; r += 8) {
+    const int j = j0 + r, i = i0 + tx;
+    tile[r][tx] = (j < n && i < n) ? ab[(size_t)j * n + i] : s_zero<T>();
+  }
+  __syncthreads();
+  T* Mb = M + (size_t)b * n * n;
+  for (int r = ty; r < 32; r += 8) {
+    const int i = i0 + r, j = j0 + tx;
+    if (i < n && j < n) Mb[(size_t)i * n + j] = scale(sub(ab[(size_t)i * n + j], tile[tx][r]), R(0.5));
+  }
+}
 
 template <typename T>
 __device__ __forceinline__ typename Sc<T>::R lg_key(T v, bool live) {
@@ -413,10 +441,12 @@ __global__ void __launch_bounds__(32) lg_finish_kernel(LgArgs<T> A, Job<T> J, in
       if (m != R(0)) sgn = {rdiv(sgn.re, m), rdiv(sgn.im, m)};
     }
     const R la = nz ? -INFINITY : ls.value();
-    J.sign[b0 + b] = sgn;
-    J.logabs[b0 + b] = la;
-    if (J.value) J.value[b0 + b] = scale(sgn, rexp(la));
-    A.flag[b] = nz ? 1 : 0;
+    if (A.primal) {
+      J.sign[b0 + b] = sgn;
+      J.logabs[b0 + b] = la;
+      if (J.value) J.value[b0 + b] = scale(sgn, rexp(la));
+    }
+    A.flag[b] = (nz ? 1 : 0) | ((A.zsign && is_zero(A.zsign[b0 + b])) ? 4 : 0);
     if (grad) {
       int* pm = A.perm + (size_t)b * n;
       for (int k = 0; k < n; ++k) pm[k] = k;
@@ -463,7 +493,7 @@ __global__ void __launch_bounds__(256) lg_grad_kernel(LgArgs<T> A, Job<T> J, int
   for (int kk = ty; kk < 32; kk += 8) {
     const int k = k0 + kk, j = j0 + tx;
     if (k < n && j < n) {
-      T v = zero ? s_zero<T>() : mul(f, tile[tx][kk]);
+      T v = zero ? s_zero<T>() : scale(mul(f, tile[tx][kk]), A.gscale);
       G[(size_t)pm[k] * n + j] = maybe_conj(J, v);
     }
   }
