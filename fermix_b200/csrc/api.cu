@@ -20,6 +20,7 @@
 #include "pf_tc.cuh"
 #include "lu_tc.cuh"
 #include "large_lu.cuh"
+#include "large_pf.cuh"
 
 namespace {
 
@@ -338,6 +339,61 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
   return FX_OK;
 }
 
+// Large-n Parlett-Reid forward (kSmallMax < n <= kPflRows, n even): the panel loop of
+// large_pf.cuh over slices of the batch, on the large-LU workspace layout.
+template <typename T>
+int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
+  constexpr int NP = PflCfg<T>::NP;
+  const int n = J.n;
+  if (!ws) return FX_ERR_WORKSPACE;
+  int64_t bs = lg_slice<T>(J.B);
+  while (bs > 1 && LgLayout<T>(bs, n).total > wsb) bs = bs / 2;
+  const LgLayout<T> Lw(bs, n);
+  if (Lw.total > wsb) return FX_ERR_WORKSPACE;
+  unsigned char* w = static_cast<unsigned char*>(ws);
+  PflArgs<T> A{};
+  A.M = reinterpret_cast<T*>(w + Lw.M);
+  A.C = reinterpret_cast<T*>(w + Lw.C);
+  A.P = reinterpret_cast<T*>(w + Lw.P);
+  A.dvec = reinterpret_cast<T*>(w + Lw.piv);
+  A.ipiv = reinterpret_cast<int*>(w + Lw.ipiv);
+  A.n = n;
+  LgArgs<T> U{};
+  U.M = A.M;
+  U.C = A.C;
+  U.P = A.P;
+  U.n = n;
+  const size_t psmem = pfl_panel_smem<T>();
+  if (cudaFuncSetAttribute((void*)&pfl_panel_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) !=
+      cudaSuccess)
+    return FX_ERR_CUDA;
+  for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
+    const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);
+    if (J.skew) {
+      lg_skew_copy_kernel<T><<<dim3((n + 31) / 32, (n + 31) / 32, cnt), 256, 0, s>>>(A.M, J.a + b0 * (int64_t)n * n, n);
+    } else if (cudaMemcpyAsync(A.M, J.a + b0 * (int64_t)n * n, (size_t)cnt * n * n * sizeof(T),
+                               cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+      return FX_ERR_CUDA;
+    }
+    for (int k0 = 0; k0 < n; k0 += 2 * NP) {
+      A.k0 = k0;
+      A.np = (n - k0) / 2 < NP ? (n - k0) / 2 : NP;
+      pfl_panel_kernel<T><<<cnt, kPflRows, psmem, s>>>(A);
+      pfl_swap_rows_kernel<T><<<dim3((n - k0 + 255) / 256, cnt), 256, 0, s>>>(A);
+      pfl_swap_cols_kernel<T><<<dim3((n - k0 + 255) / 256, cnt), 256, 0, s>>>(A);
+      const int lo = k0 + 2 * A.np;
+      if (lo < n) {
+        U.k0 = k0;
+        U.kw = 2 * A.np;
+        lg_update_kernel<T, true><<<dim3((n - lo + 63) / 64, (n - lo + 63) / 64, cnt), 256, 0, s>>>(U, lo, lo);
+      }
+    }
+    pfl_finish_kernel<T><<<cnt, 32, 0, s>>>(A, J, b0);
+    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  }
+  return FX_OK;
+}
+
 template <typename T>
 int run_det(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* a, const void* coef, int conj_out,
             int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb) {
@@ -397,15 +453,24 @@ int run_pf(cudaStream_t s, int prec, int64_t batch, int64_t n, int skew, const v
       return launch_pf_tc(s, F);
     }
   }
-  if (n > kSmallMax && mode == MODE_SLOG_GRAD) {
-    // the Parlett-Reid forward gives (sign, logabs, value); the gradient S^-T / 2 comes
-    // from the large-n Gauss-Jordan engine (same stream, the workspace reused)
+  if (n > kSmallMax) {
+    // large n: the blocked Parlett-Reid forward (n <= kPflRows; the generic kernel above),
+    // the gradient S^-T / 2 from the Gauss-Jordan engine, the Pfaffian adjugate from the
+    // generic kernel with (sign, logabs, value) rewritten by the forward -- one after the
+    // other on the same stream and workspace
     Job<T> F = J;
     F.mode = MODE_FWD;
     F.g = nullptr;
-    int e = launch_fused<T, true>(s, F, ws, wsb);
+    auto forward = [&]() { return n <= kPflRows ? run_large_pf<T>(s, F, ws, wsb) : launch_fused<T, true>(s, F, ws, wsb); };
+    if (mode == MODE_FWD) return forward();
+    if (mode == MODE_SLOG_GRAD) {
+      int e = forward();
+      if (e) return e;
+      return run_large_lu<T>(s, J, ws, wsb, true, true);
+    }
+    int e = launch_fused<T, true>(s, J, ws, wsb);
     if (e) return e;
-    return run_large_lu<T>(s, J, ws, wsb, true, true);
+    return n <= kPflRows ? run_large_pf<T>(s, F, ws, wsb) : FX_OK;
   }
   return launch_fused<T, true>(s, J, ws, wsb);
 }
@@ -434,7 +499,7 @@ size_t ws_bytes_t(int op, int64_t batch, int64_t n, int grad) {
   Plan P;
   int e = op == FX_OP_SLOGPF ? plan_fused<T, true>(batch, (int)n, mode, P) : plan_fused<T, false>(batch, (int)n, mode, P);
   const size_t generic = (e || P.in_smem) ? 0 : (size_t)P.grid * P.slot;
-  if (n > kSmallMax && (op == FX_OP_SLOGDET || grad)) {
+  if (n > kSmallMax && (op == FX_OP_SLOGDET || grad || n <= kPflRows)) {
     // the large-n engine (the det adjugate and the Pfaffian gradient also run the generic
     // kernel, one after the other on the same workspace)
     const size_t lg = lg_ws_bytes<T>(batch, (int)n);

@@ -355,10 +355,11 @@ __global__ void __launch_bounds__(256) lg_coef_kernel(LgArgs<T> A, int r_lo) {
   for (int t = 0; t < NB; ++t) cr[t] = c[t];
 }
 
-// 5. M[x][y] -= sum_s C[x][s] P[s][y] over rows [r_lo, n) x columns [c_lo, n) minus the
-// panel columns; 64 x 64 tiles, 256 threads, 4 x 4 entries per thread, one FMA chain per
-// entry in panel-column order.
-template <typename T>
+// 5. M[x][y] -= sum_s C[x][s] P[s][y] (s < kw) over rows [r_lo, n) x columns [c_lo, n)
+// minus the panel columns [k0, k0 + kw); 64 x 64 tiles, 256 threads, 4 x 4 entries per
+// thread, one FMA chain per entry in panel-column order. SKEW: only entries below the
+// diagonal are computed, and M[y][x] = -M[x][y] is written beside them.
+template <typename T, bool SKEW = false>
 __global__ void __launch_bounds__(256) lg_update_kernel(LgArgs<T> A, int r_lo, int c_lo) {
   constexpr int NB = LgCfg<T>::NB;
   constexpr int TM = 64, TN = 64;
@@ -366,6 +367,7 @@ __global__ void __launch_bounds__(256) lg_update_kernel(LgArgs<T> A, int r_lo, i
   __shared__ T sP[NB][TN];
   const int b = blockIdx.z, n = A.n, k0 = A.k0, kw = A.kw;
   const int r0 = r_lo + blockIdx.y * TM, c0 = c_lo + blockIdx.x * TN;
+  if (SKEW && c0 >= r0 + TM) return;  // tile entirely above the diagonal
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   T* Mb = A.M + (size_t)b * n * n;
   const T* Cb = A.C + (size_t)b * n * NB;
@@ -395,7 +397,8 @@ __global__ void __launch_bounds__(256) lg_update_kernel(LgArgs<T> A, int r_lo, i
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = (rv[i] && cv[j]) ? Mb[(size_t)rr[i] * n + cc[j]] : s_zero<T>();
+    for (int j = 0; j < 4; ++j)
+      acc[i][j] = (rv[i] && cv[j] && (!SKEW || rr[i] > cc[j])) ? Mb[(size_t)rr[i] * n + cc[j]] : s_zero<T>();
   for (int s = 0; s < kw; ++s) {
     T a[4], p[4];
 #pragma unroll
@@ -411,7 +414,10 @@ __global__ void __launch_bounds__(256) lg_update_kernel(LgArgs<T> A, int r_lo, i
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      if (rv[i] && cv[j]) Mb[(size_t)rr[i] * n + cc[j]] = acc[i][j];
+      if (rv[i] && cv[j] && (!SKEW || rr[i] > cc[j])) {
+        Mb[(size_t)rr[i] * n + cc[j]] = acc[i][j];
+        if (SKEW) Mb[(size_t)cc[j] * n + rr[i]] = neg(acc[i][j]);
+      }
 }
 
 // 6. (sign, logabs) from the pivots and interchanges; gradient mode also the row
