@@ -423,3 +423,44 @@ def test_register_panel_shared_and_workspace_modes(dtype, n):
     s2, l2, g = host(fx.slogpf_parts(cuda(S), skew_symmetrize=False))
     assert np.array_equal(s, s2) and np.array_equal(l, l2)
     assert relerr(g, 0.5 * np.swapaxes(np.linalg.inv(ref64(S)), -1, -2)) < tol(dtype, 3e-3, 1e-9)
+
+
+@dtypes
+def test_n300_slogpf_large_engine(dtype):
+    """n = 300 (> 256): the blocked Parlett-Reid forward and the Gauss-Jordan gradient of
+    the large-n engine; the primal of slogpf_parts / pf_parts equals slogpf's bits, and an
+    exactly singular skew input gives (0, -inf) with a zero gradient."""
+    n = 300
+    gen = np.random.default_rng(23)
+    S = skew(randn((2, n, n), dtype, gen))
+    s, l = slogpf(S)
+    ref = [pf_ref64(S[i]) for i in range(2)]
+    assert_sign(s, [r[0] for r in ref], dtype, log_tol(dtype, n))
+    assert np.max(np.abs(l - [r[1] for r in ref])) < log_tol(dtype, n)
+    s2, l2, g = host(fx.slogpf_parts(cuda(S)))
+    assert np.array_equal(s, s2) and np.array_equal(l, l2)
+    Sh = 0.5 * (ref64(S) - np.swapaxes(ref64(S), -1, -2))
+    assert relerr(g, 0.5 * np.swapaxes(np.linalg.inv(Sh), -1, -2)) < tol(dtype, 1e-3, 1e-9)
+    v1 = host(fx.pf(cuda(S)))
+    v2, _ = host(fx.pf_parts(cuda(S)))
+    assert np.array_equal(v1, v2)
+    Z = skew(randn((1, n, n), dtype, gen))
+    Z[0, 7, :] = 0.0
+    Z[0, :, 7] = 0.0
+    sz, lz, gz = host(fx.slogpf_parts(cuda(Z)))
+    assert sz[0] == 0 and lz[0] == -np.inf and np.all(np.isfinite(gz)) and not np.any(gz)
+
+
+@dtypes
+def test_n300_det_adjugate_primal_matches_forward(dtype):
+    """n = 300: det_parts runs the generic adjugate kernel and rewrites the primal with the
+    large-n forward, so det equals det_parts' value bit for bit."""
+    n = 300
+    gen = np.random.default_rng(29)
+    A = (randn((2, n, n), dtype, gen) / np.sqrt(n) + np.eye(n)).astype(dtype)
+    v1 = host(fx.det(cuda(A)))
+    v2, g = host(fx.det_parts(cuda(A)))
+    assert np.array_equal(v1, v2)
+    s64, l64 = np.linalg.slogdet(ref64(A))
+    want = np.swapaxes(np.linalg.inv(ref64(A)), -1, -2) * (s64 * np.exp(l64))[:, None, None]
+    assert relerr(g, want) < tol(dtype, 1e-3, 1e-9)
