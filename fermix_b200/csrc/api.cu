@@ -260,16 +260,22 @@ struct LgLayout {
   }
 };
 
+constexpr size_t kLgSliceBytes = (size_t)8 << 30;  // workspace aimed at per slice (8 GiB)
+
+// Matrices per slice: enough to fill the GPU (SMs x 4), no more than the batch, and the
+// workspace kept near kLgSliceBytes for large n (at least one matrix).
 template <typename T>
-int64_t lg_slice(int64_t batch) {
+int64_t lg_slice(int64_t batch, int n) {
   const DevInfo* D = dev_info();
-  const int64_t cap = (int64_t)(D ? D->sms : 148) * kLgSliceBlocks;
+  int64_t cap = (int64_t)(D ? D->sms : 148) * kLgSliceBlocks;
+  const int64_t by_mem = (int64_t)(kLgSliceBytes / LgLayout<T>(1, n).total);
+  if (by_mem < cap) cap = by_mem < 1 ? 1 : by_mem;
   return batch < cap ? batch : cap;
 }
 
 template <typename T>
 size_t lg_ws_bytes(int64_t batch, int n) {
-  return LgLayout<T>(lg_slice<T>(batch), n).total;
+  return LgLayout<T>(lg_slice<T>(batch, n), n).total;
 }
 
 // primal: write (sign, logabs, value); pf_grad: the input is skew-symmetrised when J.skew,
@@ -279,7 +285,7 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
   constexpr int NB = LgCfg<T>::NB;
   const int n = J.n;
   if (!ws) return FX_ERR_WORKSPACE;
-  int64_t bs = lg_slice<T>(J.B);
+  int64_t bs = lg_slice<T>(J.B, n);
   while (bs > 1 && LgLayout<T>(bs, n).total > wsb) bs = bs / 2;
   const LgLayout<T> Lw(bs, n);
   if (Lw.total > wsb) return FX_ERR_WORKSPACE;
@@ -339,14 +345,38 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
   return FX_OK;
 }
 
-// Large-n Parlett-Reid forward (kSmallMax < n <= kPflRows, n even): the panel loop of
+// Cluster launch of the split panel: CL blocks of 1024 threads per matrix.
+template <typename T, int CL>
+int launch_pfl_cl(cudaStream_t s, const PflArgs<T>& A, int cnt) {
+  const size_t smem = pfl_panel_cl_smem<T>();
+  void* k = (void*)&pfl_panel_cl_kernel<T, CL>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return FX_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(CL * cnt));
+  cfg.blockDim = dim3(kPflRows);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CL;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  PflArgs<T> arg = A;
+  void* args[] = {&arg};
+  return cudaLaunchKernelExC(&cfg, k, args) == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+}
+
+// Large-n Parlett-Reid forward (kSmallMax < n <= kPflMaxN, n even): the panel loop of
 // large_pf.cuh over slices of the batch, on the large-LU workspace layout.
 template <typename T>
 int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
   constexpr int NP = PflCfg<T>::NP;
   const int n = J.n;
   if (!ws) return FX_ERR_WORKSPACE;
-  int64_t bs = lg_slice<T>(J.B);
+  int64_t bs = lg_slice<T>(J.B, n);
   while (bs > 1 && LgLayout<T>(bs, n).total > wsb) bs = bs / 2;
   const LgLayout<T> Lw(bs, n);
   if (Lw.total > wsb) return FX_ERR_WORKSPACE;
@@ -378,7 +408,15 @@ int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
     for (int k0 = 0; k0 < n; k0 += 2 * NP) {
       A.k0 = k0;
       A.np = (n - k0) / 2 < NP ? (n - k0) / 2 : NP;
-      pfl_panel_kernel<T><<<cnt, kPflRows, psmem, s>>>(A);
+      const int m = n - k0;
+      if (m <= kPflRows) {
+        pfl_panel_kernel<T><<<cnt, kPflRows, psmem, s>>>(A);
+      } else {
+        const int cl = (m + kPflRows - 1) / kPflRows;
+        const int e = cl == 2 ? launch_pfl_cl<T, 2>(s, A, cnt)
+                              : (cl == 3 ? launch_pfl_cl<T, 3>(s, A, cnt) : launch_pfl_cl<T, 4>(s, A, cnt));
+        if (e) return e;
+      }
       pfl_swap_rows_kernel<T><<<dim3((n - k0 + 255) / 256, cnt), 256, 0, s>>>(A);
       pfl_swap_cols_kernel<T><<<dim3((n - k0 + 255) / 256, cnt), 256, 0, s>>>(A);
       const int lo = k0 + 2 * A.np;
@@ -454,14 +492,14 @@ int run_pf(cudaStream_t s, int prec, int64_t batch, int64_t n, int skew, const v
     }
   }
   if (n > kSmallMax) {
-    // large n: the blocked Parlett-Reid forward (n <= kPflRows; the generic kernel above),
+    // large n: the blocked Parlett-Reid forward (n <= kPflMaxN; the generic kernel above),
     // the gradient S^-T / 2 from the Gauss-Jordan engine, the Pfaffian adjugate from the
     // generic kernel with (sign, logabs, value) rewritten by the forward -- one after the
     // other on the same stream and workspace
     Job<T> F = J;
     F.mode = MODE_FWD;
     F.g = nullptr;
-    auto forward = [&]() { return n <= kPflRows ? run_large_pf<T>(s, F, ws, wsb) : launch_fused<T, true>(s, F, ws, wsb); };
+    auto forward = [&]() { return n <= kPflMaxN ? run_large_pf<T>(s, F, ws, wsb) : launch_fused<T, true>(s, F, ws, wsb); };
     if (mode == MODE_FWD) return forward();
     if (mode == MODE_SLOG_GRAD) {
       int e = forward();
@@ -470,7 +508,7 @@ int run_pf(cudaStream_t s, int prec, int64_t batch, int64_t n, int skew, const v
     }
     int e = launch_fused<T, true>(s, J, ws, wsb);
     if (e) return e;
-    return n <= kPflRows ? run_large_pf<T>(s, F, ws, wsb) : FX_OK;
+    return n <= kPflMaxN ? run_large_pf<T>(s, F, ws, wsb) : FX_OK;
   }
   return launch_fused<T, true>(s, J, ws, wsb);
 }
@@ -499,7 +537,7 @@ size_t ws_bytes_t(int op, int64_t batch, int64_t n, int grad) {
   Plan P;
   int e = op == FX_OP_SLOGPF ? plan_fused<T, true>(batch, (int)n, mode, P) : plan_fused<T, false>(batch, (int)n, mode, P);
   const size_t generic = (e || P.in_smem) ? 0 : (size_t)P.grid * P.slot;
-  if (n > kSmallMax && (op == FX_OP_SLOGDET || grad || n <= kPflRows)) {
+  if (n > kSmallMax && (op == FX_OP_SLOGDET || grad || n <= kPflMaxN)) {
     // the large-n engine (the det adjugate and the Pfaffian gradient also run the generic
     // kernel, one after the other on the same workspace)
     const size_t lg = lg_ws_bytes<T>(batch, (int)n);

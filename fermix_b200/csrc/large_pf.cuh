@@ -187,6 +187,248 @@ inline size_t pfl_panel_smem() {
          (3 * NW) * sizeof(int) + 2 * NW * sizeof(T) + 64;
 }
 
+// ---------------------------------------------------------------- cluster panel
+// 1024 < n - k0 <= 4096: the panel's rows split over a cluster of CL blocks (1024 rows
+// each). Every block keeps its rows' pair factors and a full copy of the position
+// bookkeeping; the pivot search combines the blocks' candidates through distributed
+// shared memory, and the pivot rows' factors are read from the block that owns them. Two
+// cluster barriers per pair step, executed by every thread of every block.
+constexpr int kPflMaxN = 4 * kPflRows;
+
+__device__ __forceinline__ uint32_t cl_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cl_sync() {
+  asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+// shared::cluster address of this block's shared variable p as seen in block `rank`
+__device__ __forceinline__ uint32_t cl_map(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(umma::smem_u32(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ float cl_ld(uint32_t a, float*) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ double cl_ld(uint32_t a, double*) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ int cl_ld(uint32_t a, int*) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+template <typename R>
+__device__ __forceinline__ cplx<R> cl_ld(uint32_t a, cplx<R>*) {
+  return {cl_ld(a, (R*)nullptr), cl_ld(a + (uint32_t)sizeof(R), (R*)nullptr)};
+}
+template <typename V>
+__device__ __forceinline__ V cl_get(const V* p, uint32_t rank) {
+  return cl_ld(cl_map(p, rank), (V*)nullptr);
+}
+
+template <typename T>
+struct PflClSlot {
+  typename Sc<T>::R key[2];
+  int row[2], fi[2];
+  T val[2], fval[2];
+};
+
+template <typename T, int CL>
+__global__ void __launch_bounds__(kPflRows) pfl_panel_cl_kernel(PflArgs<T> A) {
+  typedef typename Sc<T>::R R;
+  constexpr int NP = PflCfg<T>::NP, WL = 2 * NP + 1;
+  constexpr int NW = kPflRows / 32;
+  extern __shared__ __align__(16) unsigned char smem[];
+  T* W = reinterpret_cast<T*>(smem);                               // [1024][WL] this block's rows
+  PflClSlot<T>* cs = reinterpret_cast<PflClSlot<T>*>(W + (size_t)kPflRows * WL);  // block candidate
+  T* wval = reinterpret_cast<T*>(cs + 1);                          // [2][NW] warp candidates' values
+  R* wkey = reinterpret_cast<R*>(wval + 2 * NW);                   // [NW]
+  int* wrow = reinterpret_cast<int*>(wkey + NW);                   // [NW]
+  int* wfi = wrow + NW;                                            // [NW]
+  int* at = wfi + NW;                                              // [m] position offset -> row offset
+  int* pof = at + kPflMaxN;                                        // [m] row offset -> position offset
+  const uint32_t rank = cl_rank();
+  const int b = blockIdx.x / CL, n = A.n, k0 = A.k0, np = A.np;
+  const int m = n - k0;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int xr = (int)rank * kPflRows + tid;  // this thread's row offset
+  const bool have = xr < m;
+  T* Mb = A.M + (size_t)b * n * n;
+  for (int i = tid; i < m; i += kPflRows) {
+    at[i] = i;
+    pof[i] = i;
+  }
+  bool unas = have;
+  cl_sync();
+  for (int s = 0; s < np; ++s) {
+    const int par = s & 1;
+    const int c = 2 * s;
+    const int a = at[c];
+    const uint32_t ao = (uint32_t)(a / kPflRows);
+    const T* Wa = W + (a % kPflRows) * WL;
+    if (xr == a) unas = false;
+    T colA = s_zero<T>();
+    if (have) colA = Mb[(size_t)(k0 + xr) * n + k0 + a];
+    for (int t = 0; t < s; ++t) {
+      const T wa = cl_get(Wa + 2 * t, ao), ta = cl_get(Wa + 2 * t + 1, ao);
+      if (have) {
+        colA = fma_(W[tid * WL + 2 * t + 1], wa, colA);
+        colA = fms(colA, W[tid * WL + 2 * t], ta);
+      }
+    }
+    R best = unas ? abs1(colA) : R(-1);
+    if (!(best >= R(0))) best = R(-1);
+    int bi = (unas && best >= R(0)) ? xr : 0x7fffffff;
+    T bv = colA;
+    int fi = unas ? xr : 0x7fffffff;
+    T fv = colA;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const R ob = __shfl_xor_sync(0xffffffffu, best, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      const T ov = shfl_idx(bv, lane ^ off);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+        bv = ov;
+      }
+      const int of = __shfl_xor_sync(0xffffffffu, fi, off);
+      const T ofv = shfl_idx(fv, lane ^ off);
+      if (of < fi) {
+        fi = of;
+        fv = ofv;
+      }
+    }
+    if (lane == 0) {
+      wkey[warp] = best;
+      wrow[warp] = bi;
+      wfi[warp] = fi;
+      wval[warp] = bv;
+      wval[NW + warp] = fv;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // this block's candidate: lane w takes warp w's (NW == 32)
+      best = wkey[lane];
+      bi = wrow[lane];
+      bv = wval[lane];
+      fi = wfi[lane];
+      fv = wval[NW + lane];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const R ob = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        const T ov = shfl_idx(bv, lane ^ off);
+        if (ob > best || (ob == best && oi < bi)) {
+          best = ob;
+          bi = oi;
+          bv = ov;
+        }
+        const int of = __shfl_xor_sync(0xffffffffu, fi, off);
+        const T ofv = shfl_idx(fv, lane ^ off);
+        if (of < fi) {
+          fi = of;
+          fv = ofv;
+        }
+      }
+      if (lane == 0) {
+        cs->key[par] = best;
+        cs->row[par] = bi;
+        cs->val[par] = bv;
+        cs->fi[par] = fi;
+        cs->fval[par] = fv;
+      }
+    }
+    cl_sync();
+    // the cluster's pivot: the blocks' candidates in block order
+    R pb = R(-1);
+    int p = 0x7fffffff, pfi = 0x7fffffff;
+    T pv = s_zero<T>(), pfv = s_zero<T>();
+#pragma unroll
+    for (int r = 0; r < CL; ++r) {
+      const R ob = cl_get(&cs->key[par], (uint32_t)r);
+      const int oi = cl_get(&cs->row[par], (uint32_t)r);
+      if (ob > pb || (ob == pb && oi < p)) {
+        pb = ob;
+        p = oi;
+        pv = cl_get(&cs->val[par], (uint32_t)r);
+      }
+      const int of = cl_get(&cs->fi[par], (uint32_t)r);
+      if (of < pfi) {
+        pfi = of;
+        pfv = cl_get(&cs->fval[par], (uint32_t)r);
+      }
+    }
+    if (p == 0x7fffffff) {
+      p = pfi;
+      pv = pfv;
+    }
+    const T d = neg(pv);
+    const T inv = recip(d);
+    if (xr == p) unas = false;
+    const uint32_t po = (uint32_t)(p / kPflRows);
+    const T* Wp = W + (p % kPflRows) * WL;
+    T colP = s_zero<T>();
+    if (have) colP = Mb[(size_t)(k0 + xr) * n + k0 + p];
+    for (int t = 0; t < s; ++t) {
+      const T wp = cl_get(Wp + 2 * t, po), tp = cl_get(Wp + 2 * t + 1, po);
+      if (have) {
+        colP = fma_(W[tid * WL + 2 * t + 1], wp, colP);
+        colP = fms(colP, W[tid * WL + 2 * t], tp);
+      }
+    }
+    if (have) {
+      W[tid * WL + 2 * s] = unas ? colP : s_zero<T>();
+      W[tid * WL + 2 * s + 1] = unas ? neg(mul(colA, inv)) : s_zero<T>();
+    }
+    if (tid == 0) {
+      const int q = pof[p];
+      if (rank == 0) {
+        A.ipiv[(size_t)b * n + k0 + c + 1] = k0 + q;
+        A.dvec[(size_t)b * (n / 2) + (k0 + c) / 2] = d;
+      }
+      if (q != c + 1) {
+        const int y = at[c + 1];
+        at[c + 1] = p;
+        at[q] = y;
+        pof[p] = c + 1;
+        pof[y] = q;
+      }
+    }
+    cl_sync();
+  }
+  if (have) {
+    constexpr int LD = LgCfg<T>::NB;
+    const int pos = k0 + pof[xr];
+    T* cr = A.C + ((size_t)b * n + pos) * LD;
+    T* pb = A.P + (size_t)b * LD * n;
+#pragma unroll
+    for (int t = 0; t < NP; ++t) {
+      const T w = t < np ? W[tid * WL + 2 * t] : s_zero<T>();
+      const T tau = t < np ? W[tid * WL + 2 * t + 1] : s_zero<T>();
+      cr[2 * t] = neg(tau);
+      cr[2 * t + 1] = w;
+      pb[(size_t)(2 * t) * n + pos] = w;
+      pb[(size_t)(2 * t + 1) * n + pos] = tau;
+    }
+  }
+}
+
+template <typename T>
+inline size_t pfl_panel_cl_smem() {
+  typedef typename Sc<T>::R R;
+  constexpr int NW = kPflRows / 32;
+  return (size_t)kPflRows * (2 * PflCfg<T>::NP + 1) * sizeof(T) + sizeof(PflClSlot<T>) + 2 * NW * sizeof(T) +
+         NW * sizeof(R) + 2 * NW * sizeof(int) + 2 * kPflMaxN * sizeof(int) + 64;
+}
+
 // 2a. the panel's row interchanges on columns [k0, n)
 template <typename T>
 __global__ void __launch_bounds__(256) pfl_swap_rows_kernel(PflArgs<T> A) {
