@@ -4,8 +4,9 @@
  * stream-ordered (no host synchronisation), allocates nothing, and returns 0 or one of
  * the FX_ERR_* codes; numerical singularity is not an error (it gives sign 0 and
  * logabs -inf). The caller owns all memory: inputs, outputs and the optional
- * workspace (size from fermix_workspace_bytes; only matrices too large for one
- * block's shared memory use it).
+ * workspace (size from fermix_workspace_bytes: the blocked engines for n > 256 keep
+ * their matrices there, a slice of the batch at a time; smaller n uses it only when a
+ * matrix does not fit in one block's shared memory).
  *
  * Arrays are C-contiguous: a (batch, n, n) row-major, complex values interleaved
  * (re, im) as in numpy / torch / XLA; sign, value and coef have the input dtype,
