@@ -31,7 +31,7 @@ struct PfTcSmem {
   float v[8][kTcN];  // v_t[x] = -col_a[x] / d_t
   float whi[kTcN * 16], wlo[kTcN * 16];  // MMA A operand (K-major, interleaved), TF32 hi / lo
   float bhi[kTcN * 16], blo[kTcN * 16];  // MMA B operand
-  float app[16][17];                     // A_PP of the panel, then A_PP^-1
+  __align__(16) float app[16][20];       // A_PP of the panel, then A_PP^-1 (16-byte rows)
   float cand_a[4], cand_c[4];            // per-warp pivot candidates: |value|, value
   int cand_i[4], cand_f[4];              // index, first live row
   int at[kTcN], pof[kTcN];               // position -> row, row -> position (virtual pivoting)
@@ -239,23 +239,45 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
         }
       }
       FX_TOC(tq, 9);
-      // ---- MMA operands: W[x] = (u_t, v_t), B[x] = sigma(x) d_t (v_t, -u_t)
+      // ---- gradient mode: the pivot block A_PP (rows of the pivot threads) for its inverse,
+      // and the output-lane mask of the pivot rows
+      int kx = -1;
+      if (GRAD) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          if (k < 2 * np && S.pidx[k] == x) kx = k;
+        if (kx >= 0) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < 2 * np) S.app[kx][j] = s0[j];
+        }
+        const unsigned notP = __ballot_sync(0xffffffffu, kx < 0);
+        if (lane == 0) S.dis[warp] = notP;
+      }
+      // ---- MMA operands: W[x] = (u_t, v_t), B[x] = sigma(x) d_t (v_t, -u_t), 16-byte stores
       {
         const float sig = swept_before ? -1.f : 1.f;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const int t = k >> 1;
-          float w = 0.f, z = 0.f;
-          if (t < np) {
-            w = (k & 1) ? vr[t] : ur[t];
-            z = (k & 1) ? -sig * dr[t] * ur[t] : sig * dr[t] * vr[t];
+        for (int q = 0; q < 4; ++q) {
+          float wh[4], wl[4], zh[4], zl[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int k = 4 * q + e, t = k >> 1;
+            float w = 0.f, z = 0.f;
+            if (t < np) {
+              w = (k & 1) ? vr[t] : ur[t];
+              z = (k & 1) ? -sig * dr[t] * ur[t] : sig * dr[t] * vr[t];
+            }
+            wh[e] = umma::tf32_round(w);
+            wl[e] = umma::tf32_round(w - wh[e]);
+            zh[e] = umma::tf32_round(z);
+            zl[e] = umma::tf32_round(z - zh[e]);
           }
-          const uint32_t off = umma::kmajor_offset(x, k, kTcSlab) / 4;
-          const float wh = umma::tf32_round(w), zh = umma::tf32_round(z);
-          S.whi[off] = wh;
-          S.wlo[off] = umma::tf32_round(w - wh);
-          S.bhi[off] = zh;
-          S.blo[off] = umma::tf32_round(z - zh);
+          const uint32_t off = umma::kmajor_offset(x, 4 * q, kTcSlab) / 4;
+          *reinterpret_cast<float4*>(&S.whi[off]) = make_float4(wh[0], wh[1], wh[2], wh[3]);
+          *reinterpret_cast<float4*>(&S.wlo[off]) = make_float4(wl[0], wl[1], wl[2], wl[3]);
+          *reinterpret_cast<float4*>(&S.bhi[off]) = make_float4(zh[0], zh[1], zh[2], zh[3]);
+          *reinterpret_cast<float4*>(&S.blo[off]) = make_float4(zl[0], zl[1], zl[2], zl[3]);
         }
       }
       umma::fence_proxy_async_smem();
@@ -275,6 +297,8 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
         }
         umma::mma_commit(&S.mbar);
       }
+      // gradient mode: warp 0 inverts A_PP while the tensor core runs the update
+      if (GRAD && warp == 0) tc_block_inverse(S, np);
       __syncwarp();
       if (!umma::mbar_wait(&S.mbar, phase, kTcWaitIters)) S.bad = 1;
       phase ^= 1;
@@ -286,46 +310,64 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
         //   A'_XP = A_XP A_PP^-1, A'_PP = -A_PP^-1 (16 TMEM column stores per thread),
         //   A'_PY = A_PP^-1 A_PY = A_PP^-1 (tau(y) A_YP^T), tau = -1 unswept / +1 swept y,
         // the latter as a second MMA whose output lanes are only the pivot rows.
-        int kx = -1;
+        __syncthreads();  // A_PP^-1 complete
+        FX_TOC(tq, 1);
+        float pv[16], a2[16];
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-          if (k < 2 * np && S.pidx[k] == x) kx = k;
+        for (int j = 0; j < 16; ++j) pv[j] = a2[j] = 0.f;
         if (kx >= 0) {
+          const float4* r4 = reinterpret_cast<const float4*>(S.app[kx]);
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (j < 2 * np) S.app[kx][j] = s0[j];
-        }
-        const unsigned notP = __ballot_sync(0xffffffffu, kx < 0);
-        if (lane == 0) S.dis[warp] = notP;
-        __syncthreads();
-        if (warp == 0) tc_block_inverse(S, np);
-        __syncthreads();
-        float pv[16];
-        const float tau = swept_before ? 1.f : -1.f;
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = r4[q];
+            a2[4 * q] = v.x;
+            a2[4 * q + 1] = v.y;
+            a2[4 * q + 2] = v.z;
+            a2[4 * q + 3] = v.w;
+          }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float acc = 0.f, a2 = 0.f;
-          if (j < 2 * np) {
-            if (kx >= 0) {
-              acc = -S.app[kx][j];
-              a2 = S.app[kx][j];
-            } else {
+          for (int j = 0; j < 16; ++j) pv[j] = -a2[j];
+        } else {
+          // s0 A_PP^-1: broadcast 16-byte row loads, 16 independent accumulators
 #pragma unroll
-              for (int i = 0; i < 16; ++i)
-                if (i < 2 * np) acc = fmaf(s0[i], S.app[i][j], acc);
+          for (int i = 0; i < 16; ++i) {
+            if (i < 2 * np) {
+              const float4* r4 = reinterpret_cast<const float4*>(S.app[i]);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 v = r4[q];
+                pv[4 * q] = fmaf(s0[i], v.x, pv[4 * q]);
+                pv[4 * q + 1] = fmaf(s0[i], v.y, pv[4 * q + 1]);
+                pv[4 * q + 2] = fmaf(s0[i], v.z, pv[4 * q + 2]);
+                pv[4 * q + 3] = fmaf(s0[i], v.w, pv[4 * q + 3]);
+              }
             }
           }
-          pv[j] = acc;
-          const float b2 = tau * s0[j];
-          const uint32_t off = umma::kmajor_offset(x, j, kTcSlab) / 4;
-          const float ah = umma::tf32_round(a2), bh = umma::tf32_round(b2);
-          S.whi[off] = ah;
-          S.wlo[off] = umma::tf32_round(a2 - ah);
-          S.bhi[off] = bh;
-          S.blo[off] = umma::tf32_round(b2 - bh);
+        }
+        const float tau = swept_before ? 1.f : -1.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float ah[4], al[4], bh[4], bl[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = 4 * q + e;
+            const bool on = j < 2 * np;
+            if (!on) pv[j] = 0.f;
+            const float av = on ? a2[j] : 0.f, bv = on ? tau * s0[j] : 0.f;
+            ah[e] = umma::tf32_round(av);
+            al[e] = umma::tf32_round(av - ah[e]);
+            bh[e] = umma::tf32_round(bv);
+            bl[e] = umma::tf32_round(bv - bh[e]);
+          }
+          const uint32_t off = umma::kmajor_offset(x, 4 * q, kTcSlab) / 4;
+          *reinterpret_cast<float4*>(&S.whi[off]) = make_float4(ah[0], ah[1], ah[2], ah[3]);
+          *reinterpret_cast<float4*>(&S.wlo[off]) = make_float4(al[0], al[1], al[2], al[3]);
+          *reinterpret_cast<float4*>(&S.bhi[off]) = make_float4(bh[0], bh[1], bh[2], bh[3]);
+          *reinterpret_cast<float4*>(&S.blo[off]) = make_float4(bl[0], bl[1], bl[2], bl[3]);
         }
         umma::fence_proxy_async_smem();
         tc_sync();
+        FX_TOC(tq, 2);
         if (tid == 0) {
           const uint32_t idesc = umma::idesc_tf32(kTcN, kTcN, false);
           const uint32_t dis[4] = {S.dis[0], S.dis[1], S.dis[2], S.dis[3]};
@@ -345,11 +387,13 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
         if (!umma::mbar_wait(&S.mbar, phase, kTcWaitIters)) S.bad = 1;
         phase ^= 1;
         umma::fence_after_sync();
+        FX_TOC(tq, 3);
 #pragma unroll
         for (int j = 0; j < 16; ++j)
           if (j < 2 * np) umma::tmem_st1(trow + S.pidx[j], __float_as_uint(pv[j]));
         umma::tmem_wait_st();
         tc_sync();
+        FX_TOC(tq, 4);
       }
       // the panel's pivots are swept now
       S.isP[x] = 0;
