@@ -67,13 +67,6 @@ __device__ __forceinline__ void split3(float v, float& hi, float& mid, float& lo
   lo = r - mid;
 }
 
-// Order key of a pivot candidate: 0 = not a candidate, 1 = NaN (a candidate only when
-// every candidate is NaN), else |v| ordered as its bit pattern, shifted above 1.
-__device__ __forceinline__ unsigned piv_key(float v, bool live) {
-  if (!live) return 0u;
-  if (v != v) return 1u;
-  return __float_as_uint(fabsf(v)) + 2u;
-}
 
 template <int NR, bool GRAD>
 __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float> J) {

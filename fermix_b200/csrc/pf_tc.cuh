@@ -32,8 +32,8 @@ struct PfTcSmem {
   float whi[kTcN * 16], wlo[kTcN * 16];  // MMA A operand (K-major, interleaved), TF32 hi / lo
   float bhi[kTcN * 16], blo[kTcN * 16];  // MMA B operand
   __align__(16) float app[16][20];       // A_PP of the panel, then A_PP^-1 (16-byte rows)
-  float cand_a[4], cand_c[4];            // per-warp pivot candidates: |value|, value
-  int cand_i[4], cand_f[4];              // index, first live row
+  uint4 pcand[4];                        // per-warp pivot candidates: key, row, -, value bits
+  int cand_f[4];                         // scratch (the singular flag at the end)
   int at[kTcN], pof[kTcN];               // position -> row, row -> position (virtual pivoting)
   int pidx[16];                          // the panel's pivot rows a_0, p_0, a_1, p_1, ...
   unsigned char isP[kTcN];
@@ -160,48 +160,26 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
               colA = fmaf(-ur[t], r1, colA);
               colA = fmaf(-vr[t], r2, colA);
             }
-          // pivot: largest |colA| over the unassigned rows (first occurrence)
-          float best = live ? fabsf(colA) : -1.f;
-          int bi = live ? x : 0x7fffffff;
-          float bc = colA;
-          int fl = live ? x : 0x7fffffff;
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) {
-            const float ob = __shfl_xor_sync(0xffffffffu, best, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            const float oc = __shfl_xor_sync(0xffffffffu, bc, off);
-            if (ob > best || (ob == best && oi < bi)) {
-              best = ob;
-              bi = oi;
-              bc = oc;
-            }
-            fl = min(fl, __shfl_xor_sync(0xffffffffu, fl, off));
-          }
-          if (lane == 0) {
-            S.cand_a[warp] = best;
-            S.cand_i[warp] = bi;
-            S.cand_c[warp] = bc;
-            S.cand_f[warp] = fl;
-          }
+          // pivot: largest |colA| over the unassigned rows (first occurrence): per warp two
+          // redux.sync on the packed key, then the four warps' candidates
+          const unsigned key = piv_key(colA, live);
+          const unsigned km = __reduce_max_sync(0xffffffffu, key);
+          const int wi = __reduce_min_sync(0xffffffffu, key == km ? x : 0x7fffffff);
+          if (x == wi) S.pcand[warp] = make_uint4(km, (unsigned)wi, 0u, __float_as_uint(colA));
           __syncthreads();
-          float pb = S.cand_a[0], pc = S.cand_c[0];
-          int p = S.cand_i[0], pf = S.cand_f[0];
+          uint4 hd[4];
 #pragma unroll
-          for (int w = 1; w < 4; ++w) {
-            const float ob = S.cand_a[w];
-            const int oi = S.cand_i[w];
-            if (ob > pb || (ob == pb && oi < p)) {
-              pb = ob;
-              p = oi;
-              pc = S.cand_c[w];
+          for (int w = 0; w < 4; ++w) hd[w] = S.pcand[w];
+          unsigned bk = hd[0].x, bp = hd[0].y, bvb = hd[0].w;
+#pragma unroll
+          for (int w = 1; w < 4; ++w)
+            if (hd[w].x > bk || (hd[w].x == bk && hd[w].y < bp)) {
+              bk = hd[w].x;
+              bp = hd[w].y;
+              bvb = hd[w].w;
             }
-            pf = min(pf, S.cand_f[w]);
-          }
-          float d = -pc;
-          if (p == 0x7fffffff) {  // nothing compares (NaN column): the first live row, pivot NaN
-            p = pf;
-            d = __int_as_float(0x7fc00000);
-          }
+          const int p = (int)bp;
+          const float d = -__uint_as_float(bvb);  // all candidates NaN: the first one, d = NaN
           const float inv = d == 0.f ? 0.f : __fdiv_rn(1.f, d);
           if (x == p) live = false;
           float colP = __uint_as_float(umma::tmem_ld1(trow + p));

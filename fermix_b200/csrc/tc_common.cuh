@@ -18,6 +18,15 @@ __device__ __forceinline__ void tc_sync() {
   umma::fence_after_sync();
 }
 
+// Order key of a pivot candidate for redux.sync: 0 = not a candidate, 1 = NaN (a
+// candidate only when every candidate is NaN), else |v| ordered as its bit pattern,
+// shifted above 1.
+__device__ __forceinline__ unsigned piv_key(float v, bool live) {
+  if (!live) return 0u;
+  if (v != v) return 1u;
+  return __float_as_uint(fabsf(v)) + 2u;
+}
+
 // Start pulling an n x n float32 matrix into L2 (bulk prefetch, 16 KB pieces). Skipped
 // unless the address and size are 16-byte multiples, as the instruction requires.
 __device__ __forceinline__ void tc_prefetch_l2(const float* p, int n) {
