@@ -393,9 +393,13 @@ int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
   U.C = A.C;
   U.P = A.P;
   U.n = n;
-  const size_t psmem = pfl_panel_smem<T>();
-  if (cudaFuncSetAttribute((void*)&pfl_panel_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) !=
-      cudaSuccess)
+  // n <= 512: 512-row panel blocks with twice the pairs (a wider, less memory-bound update)
+  const bool small = n <= 512;
+  constexpr int NPS = PflCfg<T>::NP_SMALL;
+  const int np_max = small ? NPS : NP;
+  const size_t psmem = small ? pfl_panel_smem<T, NPS, 512>() : pfl_panel_smem<T, NP, kPflRows>();
+  void* pk = small ? (void*)&pfl_panel_kernel<T, NPS, 512> : (void*)&pfl_panel_kernel<T, NP, kPflRows>;
+  if (cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) != cudaSuccess)
     return FX_ERR_CUDA;
   for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
     const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);
@@ -405,12 +409,14 @@ int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
                                cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
       return FX_ERR_CUDA;
     }
-    for (int k0 = 0; k0 < n; k0 += 2 * NP) {
+    for (int k0 = 0; k0 < n; k0 += 2 * np_max) {
       A.k0 = k0;
-      A.np = (n - k0) / 2 < NP ? (n - k0) / 2 : NP;
+      A.np = (n - k0) / 2 < np_max ? (n - k0) / 2 : np_max;
       const int m = n - k0;
-      if (m <= kPflRows) {
-        pfl_panel_kernel<T><<<cnt, kPflRows, psmem, s>>>(A);
+      if (small) {
+        pfl_panel_kernel<T, NPS, 512><<<cnt, 512, psmem, s>>>(A);
+      } else if (m <= kPflRows) {
+        pfl_panel_kernel<T, NP, kPflRows><<<cnt, kPflRows, psmem, s>>>(A);
       } else {
         const int cl = (m + kPflRows - 1) / kPflRows;
         const int e = cl == 2 ? launch_pfl_cl<T, 2>(s, A, cnt)

@@ -27,7 +27,8 @@ constexpr int kPflRows = 1024;  // rows per panel block (one thread each): n <= 
 
 template <typename T>
 struct PflCfg {
-  static constexpr int NP = sizeof(T) <= 8 ? 8 : 4;  // pairs per panel
+  static constexpr int NP = sizeof(T) <= 8 ? 8 : 4;         // pairs per panel, 1024-row blocks
+  static constexpr int NP_SMALL = LgCfg<T>::NB / 2;         // pairs per panel, n <= 512 (512-row blocks)
 };
 
 template <typename T>
@@ -40,17 +41,18 @@ struct PflArgs {
   int n, k0, np;
 };
 
-// 1. panel: block b factors pairs k0 / 2 .. k0 / 2 + np - 1 of matrix b
-template <typename T>
-__global__ void __launch_bounds__(kPflRows) pfl_panel_kernel(PflArgs<T> A) {
+// 1. panel: block b factors pairs k0 / 2 .. k0 / 2 + np - 1 of matrix b (ROWS threads,
+// n - k0 <= ROWS; NP pairs at most)
+template <typename T, int NP, int ROWS>
+__global__ void __launch_bounds__(ROWS) pfl_panel_kernel(PflArgs<T> A) {
   typedef typename Sc<T>::R R;
-  constexpr int NP = PflCfg<T>::NP, WL = 2 * NP + 1;
-  constexpr int NW = kPflRows / 32;
+  constexpr int WL = 2 * NP + 1;
+  constexpr int NW = ROWS / 32;
   extern __shared__ __align__(16) unsigned char smem[];
-  T* W = reinterpret_cast<T*>(smem);                          // [m][WL] pair factors by row offset
-  int* at = reinterpret_cast<int*>(W + (size_t)kPflRows * WL);  // [m] position offset -> row offset
-  int* pof = at + kPflRows;                                   // [m] row offset -> position offset
-  R* skey = reinterpret_cast<R*>(pof + kPflRows);             // [NW] best |colA| per warp
+  T* W = reinterpret_cast<T*>(smem);                      // [m][WL] pair factors by row offset
+  int* at = reinterpret_cast<int*>(W + (size_t)ROWS * WL);  // [m] position offset -> row offset
+  int* pof = at + ROWS;                                   // [m] row offset -> position offset
+  R* skey = reinterpret_cast<R*>(pof + ROWS);                 // [NW] best |colA| per warp
   int* srow = reinterpret_cast<int*>(skey + NW);              // [NW] its row offset
   int* sfir = srow + NW;                                      // [NW] first unassigned row offset
   T* sval = reinterpret_cast<T*>(sfir + NW + (NW % 4));       // [2][NW] colA of the best / first
@@ -179,12 +181,12 @@ __global__ void __launch_bounds__(kPflRows) pfl_panel_kernel(PflArgs<T> A) {
   }
 }
 
-template <typename T>
+template <typename T, int NP, int ROWS>
 inline size_t pfl_panel_smem() {
   typedef typename Sc<T>::R R;
-  constexpr int NW = kPflRows / 32;
-  return (size_t)kPflRows * (2 * PflCfg<T>::NP + 1) * sizeof(T) + 2 * kPflRows * sizeof(int) + NW * sizeof(R) +
-         (3 * NW) * sizeof(int) + 2 * NW * sizeof(T) + 64;
+  constexpr int NW = ROWS / 32;
+  return (size_t)ROWS * (2 * NP + 1) * sizeof(T) + 2 * ROWS * sizeof(int) + NW * sizeof(R) + (3 * NW) * sizeof(int) +
+         2 * NW * sizeof(T) + 64;
 }
 
 // ---------------------------------------------------------------- cluster panel
