@@ -28,18 +28,22 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "slogdet/slogpf matrices/sec fwd & fwd+bwd at 1-8 B200; % of roofline"
-KERNEL = {"slogpf": "pf_fused_kernel", "slogdet": "lu_fused_kernel"}
 SMALL_KERNEL = {"slogpf": "pf_small_kernel", "slogdet": "lu_small_kernel"}
 TC_KERNEL = {"slogpf": "pf_tc_kernel", "slogdet": "lu_tc_kernel"}
 
 
 def kernel_name(a):
-    """The kernel the library dispatches this workload to: the tensor-memory kernels for
-    float32 / tf32x3 with 8 <= n <= 128 (odd n aside for slogpf), the register-panel
-    kernels up to n = 256, the one-block-per-matrix generic kernels above."""
-    if a.dtype == "f32" and a.prec == "tf32x3" and 8 <= a.n <= 128 and not (a.op == "slogpf" and a.n % 2):
-        return TC_KERNEL[a.op]
-    return (SMALL_KERNEL if a.n <= 256 else KERNEL)[a.op]
+    """The dominant kernel of this workload: the tensor-memory kernels for float32 /
+    tf32x3 (slogpf 8 <= n <= 128, even n; slogdet 8 <= n <= 256), the register-panel
+    kernels otherwise up to n = 256, and above that the blocked engines' tiled update."""
+    if a.dtype == "f32" and a.prec == "tf32x3" and a.n >= 8:
+        if a.op == "slogpf" and a.n <= 128 and a.n % 2 == 0:
+            return TC_KERNEL[a.op]
+        if a.op == "slogdet" and a.n <= 256:
+            return TC_KERNEL[a.op]
+    if a.n <= 256:
+        return SMALL_KERNEL[a.op]
+    return "lg_update_kernel"
 
 
 def parse():
@@ -57,6 +61,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-sample", type=int, default=256, help="matrices in the CPU baseline sample")
     ap.add_argument("--ref-step", type=int, default=16, help="matrices per step of the reference arm")
+    ap.add_argument("--gather", type=int, default=0, metavar="SITES",
+                    help="slogdet only: matrices are rows of a shared (SITES x n) phi picked by random occupations "
+                         "(fermix_slogdet_gather, configuration 3's caller step); L2 flushed between timed steps")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
@@ -64,7 +71,8 @@ def parse():
 
 def workload_name(a):
     what = "fwd" if a.fwd_only else "fwd+VJP(logabs)"
-    return f"{a.op} {what} {a.dtype} B={a.batch}/GPU n={a.n} prec={a.prec}"
+    g = f" gathered from phi {a.gather}x{a.n}" if a.gather else ""
+    return f"{a.op} {what} {a.dtype} B={a.batch}/GPU n={a.n} prec={a.prec}{g}"
 
 
 def flops_bytes(a):
@@ -77,7 +85,34 @@ def flops_bytes(a):
     else:
         fl = (1.0 / 3.0 if a.fwd_only else 5.0 / 3.0) * n**3
     by = (1 if a.fwd_only else 2) * n * n * s
+    if a.gather:
+        # the shared phi once per launch, the occupations, and the gradient written
+        by = a.gather * n * s / a.batch + n * 4 + (0 if a.fwd_only else n * n * s)
     return fl * cx, by
+
+
+# FMA-pipe peaks measured on this pool's B200s at 1965 MHz (8 independent FMA chains per
+# thread, 148 x 8 blocks of 256 threads, CUDA events)
+FFMA_TFLOPS = 72.6
+DFMA_TFLOPS = 34.1
+
+
+def compute_roofline(a, flops_per_launch, launch_s):
+    """The arithmetic pipe that bounds this workload and the fraction of it achieved:
+    the tensor cores for the tensor-memory kernels (TF32 at half the measured bf16 rate,
+    divided by the TF32 products per update), the FP32 / FP64 FMA pipes otherwise."""
+    kern = kernel_name(a)
+    achieved = flops_per_launch / launch_s / 1e12
+    if kern in TC_KERNEL.values():
+        p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+        bf16 = float(json.load(open(p))["bf16_tflops"]) if os.path.exists(p) else 1590.0
+        products = 4 if a.op == "slogdet" else 3
+        pipe, peak = f"tcgen05 kind::tf32, {products} products per update", 0.5 * bf16 / products
+    elif a.dtype in ("f32", "c64"):
+        pipe, peak = "fp32 FFMA", FFMA_TFLOPS
+    else:
+        pipe, peak = "fp64 DFMA", DFMA_TFLOPS
+    return {"pipe": pipe, "achieved_tflops": achieved, "peak_tflops": peak, "frac": achieved / peak}
 
 
 def peaks():
@@ -262,19 +297,40 @@ def main():
     B, n = a.batch, a.n
     g = torch.Generator(device=dev)
     g.manual_seed(a.seed + 1000 * rank)
-    A = torch.randn((B, n, n), generator=g, device=dev, dtype=tdt)
-    if a.op == "slogpf":
-        A = (A - A.transpose(-1, -2)).contiguous()
+    if a.gather:
+        if a.op != "slogdet" or a.gather < n:
+            raise SystemExit("--gather needs --op slogdet and SITES >= n")
+        # configuration 3: phi iid N(0, 1/sqrt(n)), sorted random n-of-SITES occupations, a
+        # duplicated row in 2 % of the samples
+        PHI = (torch.randn((a.gather, n), generator=g, device=dev, dtype=tdt) / n**0.5).contiguous()
+        OCC = torch.rand((B, a.gather), generator=g, device=dev).argsort(dim=1)[:, :n].sort(dim=1).values
+        dup = torch.rand(B, generator=g, device=dev) < 0.02
+        OCC[dup, 1] = OCC[dup, 0]
+        OCC = OCC.to(torch.int32).contiguous()
+        A = OCC  # the per-step device input
+    else:
+        A = torch.randn((B, n, n), generator=g, device=dev, dtype=tdt)
+        if a.op == "slogpf":
+            A = (A - A.transpose(-1, -2)).contiguous()
     sign = torch.empty(B, dtype=tdt, device=dev)
     logabs = torch.empty(B, dtype=rdt, device=dev)
-    G = None if a.fwd_only else torch.empty_like(A)
+    G = None if a.fwd_only else torch.empty((B, n, n), dtype=tdt, device=dev)
     op = _lib.FX_OP_SLOGPF if a.op == "slogpf" else _lib.FX_OP_SLOGDET
-    wsb = L.fermix_workspace_bytes(op, kind, B, n, 0 if a.fwd_only else 1)
+    if a.gather:
+        wsb = L.fermix_slogdet_gather_workspace_bytes(kind, prec, B, n, 0 if a.fwd_only else 1)
+    else:
+        wsb = L.fermix_workspace_bytes(op, kind, B, n, 0 if a.fwd_only else 1)
     ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
 
     def call(X, Gout):
+        if a.gather:
+            st = L.fermix_slogdet_gather(sp, kind, prec, B, n, PHI.data_ptr(), a.gather, n, X.data_ptr(), None, 0,
+                                         sign.data_ptr(), logabs.data_ptr(), None,
+                                         None if Gout is None else Gout.data_ptr(), ws.data_ptr(), wsb)
+            _lib.check(st)
+            return
         if a.op == "slogpf":
             if a.fwd_only:
                 st = L.fermix_slogpf(sp, kind, prec, B, n, 1, X.data_ptr(), sign.data_ptr(), logabs.data_ptr(),
@@ -313,13 +369,26 @@ def main():
     time.sleep(0.2)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
-    e0.record(stream)
-    for _ in range(a.steps):
-        call(A, G)
-    e1.record(stream)
-    barrier()
+    if a.gather:
+        # the gathered inputs fit in L2: flush it (write 256 MB) before every step and time
+        # each step's launch alone
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+        for f0, f1 in evs:
+            flush.fill_(1)
+            f0.record(stream)
+            call(A, G)
+            f1.record(stream)
+        barrier()
+        t_dev = sum(f0.elapsed_time(f1) for f0, f1 in evs) / 1e3
+    else:
+        e0.record(stream)
+        for _ in range(a.steps):
+            call(A, G)
+        e1.record(stream)
+        barrier()
+        t_dev = e0.elapsed_time(e1) / 1e3
     ck = clocks.stop()
-    t_dev = e0.elapsed_time(e1) / 1e3
     t_dev = max_over_ranks(t_dev)
     value = world * B * a.steps / t_dev
     ms_step = 1e3 * t_dev / a.steps
@@ -344,16 +413,22 @@ def main():
     # ---- end to end through the C ABI with host buffers
     e2e = None
     if not a.no_e2e:
-        hA = torch.empty(A.shape, dtype=tdt, pin_memory=True)
+        hA = torch.empty(A.shape, dtype=A.dtype, pin_memory=True)
         hA.copy_(A)
         dA = torch.empty_like(A)
         hS = torch.empty(B, dtype=tdt, pin_memory=True)
         hL = torch.empty(B, dtype=rdt, pin_memory=True)
-        hG = None if a.fwd_only else torch.empty(A.shape, dtype=tdt, pin_memory=True)
-        dG = None if a.fwd_only else torch.empty_like(A)
+        hG = None if a.fwd_only else torch.empty((B, n, n), dtype=tdt, pin_memory=True)
+        dG = None if a.fwd_only else torch.empty((B, n, n), dtype=tdt, device=dev)
+        hP = None
+        if a.gather:
+            hP = torch.empty(PHI.shape, dtype=tdt, pin_memory=True)
+            hP.copy_(PHI)
         ke = max(3, min(a.steps, 20))
 
         def e2e_step():
+            if hP is not None:
+                PHI.copy_(hP, non_blocking=True)
             dA.copy_(hA, non_blocking=True)
             call(dA, dG)
             hS.copy_(sign, non_blocking=True)
@@ -371,7 +446,7 @@ def main():
         f1.record(stream)
         barrier()
         t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
-        h2d = A.numel() * A.element_size()
+        h2d = A.numel() * A.element_size() + (0 if hP is None else hP.numel() * hP.element_size())
         d2h = sign.numel() * sign.element_size() + logabs.numel() * logabs.element_size()
         if hG is not None:
             d2h += hG.numel() * hG.element_size()
@@ -399,7 +474,9 @@ def main():
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": a.dtype,
-            "data": "synthetic (seeded iid N(0,1), S = A - A^T)" if a.op == "slogpf" else "synthetic (seeded iid N(0,1))",
+            "data": ("synthetic (seeded iid N(0,1), S = A - A^T)" if a.op == "slogpf" else
+                     "synthetic (seeded phi ~ N(0, 1/sqrt(n)), random sorted occupations, 2% duplicated rows)"
+                     if a.gather else "synthetic (seeded iid N(0,1))"),
             "config": {
                 "workload": workload_name(a),
                 "op": a.op,
@@ -408,9 +485,11 @@ def main():
                 "n": n,
                 "prec": a.prec,
                 "parallelism": f"batch sharded x{world}, no collective",
-                "l2": "inputs exceed L2 (no flush needed)" if B * n * n * A.element_size() > 126e6 else "inputs fit L2",
+                "l2": ("L2 flushed before every timed step" if a.gather else
+                       "inputs exceed L2 (no flush needed)" if B * n * n * A.element_size() > 126e6 else "inputs fit L2"),
             },
             "roofline": roofline,
+            "compute_roofline": compute_roofline(a, B * fl, launch_s),
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": a.steps,

@@ -13,6 +13,7 @@ from .api import (
     pf,
     pf_parts,
     slogdet,
+    slogdet_gather,
     slogdet_parts,
     slogpf,
     slogpf_parts,
@@ -28,6 +29,7 @@ __all__ = [
     "slogpf_parts",
     "det_parts",
     "pf_parts",
+    "slogdet_gather",
     "FermixFallbackWarning",
     "__version__",
 ]

@@ -24,6 +24,9 @@ SIGNATURES = {
     "fermix_slogpf": (_i, [_vp, _i, _i, _i64, _i64, _i, _vp, _vp, _vp, _vp, _vp, _sz]),
     "fermix_slogpf_grad": (_i, [_vp, _i, _i, _i64, _i64, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz]),
     "fermix_slogdet_grad_static": (_i, [_vp, _i, _i, _i64, _i64, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "fermix_slogdet_gather": (
+        _i, [_vp, _i, _i, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _sz]),
+    "fermix_slogdet_gather_workspace_bytes": (_sz, [_i, _i, _i64, _i64, _i]),
     "fermix_workspace_bytes": (_sz, [_i, _i, _i64, _i64, _i]),
     "fermix_check_prec": (_i, [_i, _i]),
     "fermix_strerror": (ctypes.c_char_p, [_i]),

@@ -38,8 +38,9 @@ class FermixFallbackWarning(UserWarning):
 
 
 # ------------------------------------------------------------------ validation
-def _prep(a):
-    """dtype / shape checks of the reference's _prep (src/fermix/api.py:24-31)."""
+def _prep(a, square=True):
+    """dtype / shape checks of the reference's _prep (src/fermix/api.py:24-31); square=False
+    only requires a matrix (the shared phi of slogdet_gather)."""
     from_host = False
     if isinstance(a, np.ndarray):
         a = torch.from_numpy(np.ascontiguousarray(a))
@@ -49,7 +50,7 @@ def _prep(a):
         from_host = True
     if a.dtype not in _KIND:
         raise TypeError(f"fermix supports float32, float64, complex64 and complex128, got {a.dtype}")
-    if a.ndim < 2 or a.shape[-1] != a.shape[-2]:
+    if a.ndim < 2 or (square and a.shape[-1] != a.shape[-2]):
         raise ValueError(f"expected (..., n, n), got {tuple(a.shape)}")
     if a.device.type != "cuda":
         if from_host and torch.cuda.is_available():
@@ -141,6 +142,28 @@ def _run(op, A, prec, *, skew=True, grad=False, coef=None, conj_out=False, adjug
                                      _ptr(ws), wsb)
     _lib.check(st)
     return sign, logabs, val, G
+
+
+def _run_gather(phi, occ, prec, *, grad=False, coef=None, conj_out=False):
+    """fermix_slogdet_gather on phi (rows, cols) and occ (B, n) int32, both contiguous
+    CUDA tensors: returns (sign, logabs, grad or None)."""
+    L = _lib.lib()
+    B, n = occ.shape
+    kind = _KIND[phi.dtype]
+    dev = phi.device
+    sign = torch.empty(B, dtype=phi.dtype, device=dev)
+    logabs = torch.empty(B, dtype=_real(phi.dtype), device=dev)
+    G = torch.empty((B, n, n), dtype=phi.dtype, device=dev) if grad else None
+    if coef is not None:
+        coef = coef.to(dtype=phi.dtype, device=dev).contiguous()
+    with torch.cuda.device(dev):
+        nbytes = L.fermix_slogdet_gather_workspace_bytes(kind, prec, B, n, int(grad))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
+        st = L.fermix_slogdet_gather(_stream_ptr(dev), kind, prec, B, n, _ptr(phi), phi.shape[0], phi.shape[1],
+                                     _ptr(occ), _ptr(coef), int(conj_out), _ptr(sign), _ptr(logabs), None, _ptr(G),
+                                     _ptr(ws), nbytes)
+    _lib.check(st)
+    return sign, logabs, G
 
 
 def _flat(a):
@@ -307,6 +330,63 @@ class _Value(torch.autograd.Function):
 
 
 # ------------------------------------------------------------------ public functions
+class _SlogGather(torch.autograd.Function):
+    """(sign, logabs) of the matrices phi[occ[b]] (rows of a shared phi), differentiable
+    in phi: the backward runs the gathered gradient kernel and adds each matrix's rows
+    of coef * A^-T into the phi rows they came from."""
+
+    @staticmethod
+    def forward(phi, occ, prec):
+        sign, logabs, _ = _run_gather(phi, occ, prec)
+        return sign, logabs
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        phi, occ, prec = inputs
+        ctx.save_for_backward(phi, occ, output[0])
+        ctx.prec = prec
+        ctx.mark_non_differentiable(output[0])
+
+    @staticmethod
+    def backward(ctx, g_sign, g_logabs):
+        phi, occ, sign = ctx.saved_tensors
+        c = _slog_coef(sign, g_sign, g_logabs, phi.is_complex())
+        _, _, G = _run_gather(phi, occ, ctx.prec, grad=True, coef=c, conj_out=True)
+        B, n = occ.shape
+        rows = torch.zeros((phi.shape[0], n), dtype=phi.dtype, device=phi.device)
+        rows.index_add_(0, occ.reshape(-1).long(), G.reshape(B * n, n))
+        dphi = torch.zeros_like(phi)
+        dphi[:, :n] = rows
+        return dphi, None, None
+
+
+def slogdet_gather(phi, occ, *, prec=None):
+    """slogdet of the matrices whose rows are gathered from a shared ``phi``: matrix
+    ``b`` is ``phi[occ[b, :], :n]`` with n = occ.shape[-1] (the QMC pattern of an orbital
+    matrix and electron occupations), without materialising the batch. ``phi`` is a 2-D
+    CUDA tensor (rows, cols >= n), ``occ`` an integer tensor of shape (..., n). Returns
+    (sign, logabs) of shape occ.shape[:-1], equal to ``slogdet(phi[occ][..., :n])`` bit for
+    bit and differentiable in ``phi``. An index outside [0, rows) makes that member NaN
+    (and is not allowed when differentiating)."""
+    phi = _prep(phi, square=False)
+    if phi.dim() != 2:
+        raise ValueError("phi must be a 2-D tensor (rows, cols)")
+    if not isinstance(occ, torch.Tensor):
+        occ = torch.as_tensor(np.asarray(occ))
+    if occ.dtype not in (torch.int32, torch.int64, torch.int16, torch.uint8):
+        raise TypeError("occ must be an integer tensor")
+    if occ.dim() < 1:
+        raise ValueError("occ must have shape (..., n)")
+    n = occ.shape[-1]
+    if phi.shape[1] < n:
+        raise ValueError(f"phi has {phi.shape[1]} columns, fewer than n = {n}")
+    batch = tuple(occ.shape[:-1])
+    p = _check_prec(phi.dtype, prec)
+    O = occ.to(device=phi.device, dtype=torch.int32).reshape(-1, n).contiguous()
+    sign, logabs = _SlogGather.apply(phi.contiguous(), O, p)
+    return sign.reshape(batch), logabs.reshape(batch)
+
+
 def slogdet(a, *, prec=None, unroll_steps=None, block=None):
     """Sign and log|det| of a batch of matrices ``a`` of shape (..., n, n)
     (src/fermix/api.py:148-174). Returns (sign, logabsdet): sign has the dtype of ``a``
@@ -314,9 +394,10 @@ def slogdet(a, *, prec=None, unroll_steps=None, block=None):
     logabsdet the corresponding real dtype -- the conventions of
     ``jnp.linalg.slogdet``. Exactly singular matrices give (0, -inf) and a zero
     gradient. ``prec`` ("tf32x3" | "ieee"; "tf32x3" only for float32 / complex64) is
-    validated as in the reference; the block updates of this build run exact IEEE FMA
-    for every dtype, which is at least as accurate as either. ``block`` (None, 32, 64,
-    128) and ``unroll_steps`` are validated launch hints."""
+    validated as in the reference: "tf32x3" on float32 with 8 <= n <= 256 runs the
+    tensor-core kernels (3 TF32 products per update, fp32 accumulation), every other
+    case IEEE FMA. ``block`` (None, 32, 64, 128) and ``unroll_steps`` are validated
+    launch hints."""
     a = _prep(a)
     _check_block(block)
     _check_unroll(unroll_steps)

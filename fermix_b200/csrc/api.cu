@@ -557,6 +557,68 @@ size_t ws_bytes_t(int op, int64_t batch, int64_t n, int grad) {
   return generic;
 }
 
+// ---------------------------------------------------------------- gathered slogdet
+// Matrix b = rows occ[b, 0 .. n) of phi (phi_rows x phi_ld, row-major), columns 0 .. n.
+template <typename T>
+__global__ void __launch_bounds__(256) gather_rows_kernel(T* M, const T* phi, int64_t ld, int64_t rows,
+                                                          const int* idx, int n) {
+  typedef typename Sc<T>::R R;
+  const int64_t b = blockIdx.y;
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (int64_t)n * n) return;
+  const int i = (int)(e / n), j = (int)(e % n);
+  const int r = idx[b * n + i];
+  T v = s_zero<T>();
+  if (r >= 0 && (int64_t)r < rows) {
+    v = phi[(int64_t)r * ld + j];
+  } else {
+    const R q = R(NAN);
+    if constexpr (Sc<T>::cx) v = {q, q};
+    else v = q;
+  }
+  M[b * (int64_t)n * n + e] = v;
+}
+
+// the tensor-memory LU reads the rows itself; otherwise the batch is gathered into the
+// front of the workspace and the regular path runs on it (its workspace behind)
+template <typename T>
+bool gather_direct(int prec, int64_t n, int mode) {
+  return std::is_same<T, float>::value && use_lu_tc(1, prec, (int)n, mode);
+}
+
+template <typename T>
+size_t gather_ws_bytes(int prec, int64_t batch, int64_t n, int grad) {
+  const int mode = grad ? MODE_SLOG_GRAD : MODE_FWD;
+  if (gather_direct<T>(prec, n, mode)) return 0;
+  return align256((size_t)batch * n * n * sizeof(T)) + ws_bytes_t<T>(FX_OP_SLOGDET, batch, n, grad);
+}
+
+template <typename T>
+int run_gather(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* phi, int64_t rows, int64_t ld,
+               const int* occ, const void* coef, int conj_out, void* sign, void* logabs, void* value, void* grad,
+               void* ws, size_t wsb) {
+  const int mode = grad ? MODE_SLOG_GRAD : MODE_FWD;
+  if (gather_direct<T>(prec, n, mode)) {
+    Job<T> J = make_job<T>(batch, n, nullptr, coef, conj_out, 0, mode, sign, logabs, value, grad);
+    J.gidx = occ;
+    J.gbase = static_cast<const T*>(phi);
+    J.gld = ld;
+    J.grows = rows;
+    if constexpr (std::is_same<T, float>::value) return launch_lu_tc(s, J);
+    return FX_ERR_DTYPE;
+  }
+  const size_t mat = align256((size_t)batch * n * n * sizeof(T));
+  if (!ws || wsb < mat) return FX_ERR_WORKSPACE;
+  T* M = static_cast<T*>(ws);
+  if (n > 0) {
+    gather_rows_kernel<T><<<dim3((unsigned)((n * n + 255) / 256), (unsigned)batch), 256, 0, s>>>(
+        M, static_cast<const T*>(phi), ld, rows, occ, (int)n);
+    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  }
+  return run_det<T>(s, prec, batch, n, M, coef, conj_out, mode, sign, logabs, value, grad,
+                    static_cast<unsigned char*>(ws) + mat, wsb - mat);
+}
+
 }  // namespace
 
 extern "C" {
@@ -624,6 +686,31 @@ int fermix_slogpf_grad(void* stream, int dtype, int prec, int64_t batch, int64_t
     return run_pf<T>(s, prec, batch, n, skew_symmetrize, a, coef, conj_out, mode, sign, logabs, value, grad,
                      workspace, workspace_bytes);
   });
+}
+
+int fermix_slogdet_gather(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* phi,
+                          int64_t phi_rows, int64_t phi_ld, const int* occ, const void* coef, int conj_out,
+                          void* sign, void* logabs, void* value, void* grad, void* workspace,
+                          size_t workspace_bytes) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (phi_rows < 0 || phi_ld < n) return FX_ERR_SHAPE;
+  if (batch == 0) return FX_OK;
+  if ((n > 0 && (!phi || !occ)) || !sign || !logabs) return FX_ERR_NULL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_gather<T>(s, prec, batch, n, phi, phi_rows, phi_ld, occ, coef, conj_out, sign, logabs, value, grad,
+                         workspace, workspace_bytes);
+  });
+}
+
+size_t fermix_slogdet_gather_workspace_bytes(int dtype, int prec, int64_t batch, int64_t n, int grad) {
+  if (validate(dtype, prec, batch, n) || batch == 0) return 0;
+  return (size_t)by_dtype(dtype, [&](auto t) -> int {
+    using T = decltype(t);
+    return (int)((gather_ws_bytes<T>(prec, batch, n, grad) + 255) / 256);
+  }) * 256;
 }
 
 size_t fermix_workspace_bytes(int op, int dtype, int64_t batch, int64_t n, int grad) {

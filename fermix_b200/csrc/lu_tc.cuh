@@ -94,9 +94,13 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
 
   for (int64_t b = blockIdx.x; b < J.B; b += gridDim.x) {
     FX_TIC(tq);
-    const float* src = J.a + b * (int64_t)n * n;
-    if (tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
-    tc_load_matrix<NR>(src, n, false, trow, x);
+    if (J.gidx) {
+      tc_load_gathered<NR>(J.gbase, J.gld, J.grows, J.gidx + b * (int64_t)n, n, trow, x);
+    } else {
+      const float* src = J.a + b * (int64_t)n * n;
+      if (tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
+      tc_load_matrix<NR>(src, n, false, trow, x);
+    }
     int mypos = x < n ? -1 : NR;  // pivot position of this row (-1: not yet pivoted)
     int myinv = 0;                  // parity of the inversions this row adds as a pivot
     if (tid == 0) S.bad = 0;

@@ -91,6 +91,54 @@ __device__ __forceinline__ void tc_load_matrix(const float* __restrict__ src, in
   umma::tmem_wait_st();
 }
 
+// As tc_load_matrix (no skew) with row x taken from base[idx[x] * ld ..] (a gathered row of
+// a shared matrix, typically L2-resident); an index outside [0, rows) fills the row with NaN.
+template <int NC = kTcN>
+__device__ __forceinline__ void tc_load_gathered(const float* __restrict__ base, int64_t ld, int64_t rows,
+                                                 const int* __restrict__ idx, int n, uint32_t trow, int x) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(base) | ((uintptr_t)ld * 4u)) & 15u) == 0;
+  int r = -1;
+  if (x < n) r = __ldg(idx + x);
+  const bool ok = r >= 0 && (int64_t)r < rows;
+  const float* row = base + (ok ? (int64_t)r * ld : 0);
+#pragma unroll 1
+  for (int c0 = 0; c0 < NC; c0 += 32) {
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = 0.f;
+    if (x < n && c0 < n) {
+      if (!ok) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          if (c0 + k < n) v[k] = __int_as_float(0x7fc00000);
+      } else if (vec) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (c0 + 4 * q < n) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(row + c0) + q);
+            v[4 * q] = t.x;
+            v[4 * q + 1] = t.y;
+            v[4 * q + 2] = t.z;
+            v[4 * q + 3] = t.w;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          if (c0 + k < n) v[k] = __ldg(row + c0 + k);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = __float_as_uint(v[8 * q + j]);
+      umma::tmem_st8(trow + c0 + 8 * q, w);
+    }
+  }
+  umma::tmem_wait_st();
+}
+
 // dst[x * n + c] = f * TMEM[x][c] for c < n (zero when zero_out), thread x = row x; each
 // warp writes its own 32 rows, 32 columns at a time (16-byte stores when aligned).
 __device__ __forceinline__ void tc_store_rows(float* __restrict__ dst, int n, float f, bool zero_out,

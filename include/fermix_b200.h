@@ -90,6 +90,20 @@ int fermix_slogpf_grad(void* stream, int dtype, int prec, int64_t batch, int64_t
                        const void* a, const void* coef, int conj_out, int adjugate, void* sign, void* logabs,
                        void* value, void* grad, void* workspace, size_t workspace_bytes);
 
+/* slogdet of gathered matrices (no reference counterpart; the fused gather of the QMC
+ * caller in the reference's README): matrix b is rows occ[b * n + i] (int32, i < n) of phi
+ * (phi_rows x phi_ld row-major, same dtype), columns 0 .. n - 1, so that the batch is
+ * never materialised. grad == NULL: the forward of fermix_slogdet; otherwise also the
+ * per-matrix gradient coef * A^-T as fermix_slogdet_grad (adjugate 0). An index outside
+ * [0, phi_rows) makes that matrix NaN. Results equal fermix_slogdet / _grad on the
+ * materialised batch bit for bit. Workspace: fermix_slogdet_gather_workspace_bytes (0 for
+ * float32 tf32x3 with 8 <= n <= 256, where the tensor-memory kernel reads the rows). */
+int fermix_slogdet_gather(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* phi,
+                          int64_t phi_rows, int64_t phi_ld, const int* occ, const void* coef, int conj_out,
+                          void* sign, void* logabs, void* value, void* grad, void* workspace,
+                          size_t workspace_bytes);
+size_t fermix_slogdet_gather_workspace_bytes(int dtype, int prec, int64_t batch, int64_t n, int grad);
+
 /* Size of the fixed device array fermix_slogdet_grad_static uses instead of a workspace
  * (16 MiB, one copy per device, part of the library's device image). */
 #define FX_STATIC_SCRATCH_BYTES (16u << 20)
