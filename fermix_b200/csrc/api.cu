@@ -250,7 +250,7 @@ struct LgLayout {
     M = o;    o = align256(o + (size_t)bs * n * n * sizeof(T));
     C = o;    o = align256(o + (size_t)bs * n * NB * sizeof(T));
     P = o;    o = align256(o + (size_t)bs * NB * n * sizeof(T));
-    LU = o;   o = align256(o + (size_t)bs * 2 * NB * NB * sizeof(T));
+    LU = o;   o = align256(o + (size_t)bs * 3 * NB * NB * sizeof(T));
     piv = o;  o = align256(o + (size_t)bs * n * sizeof(T));
     ipiv = o; o = align256(o + (size_t)bs * n * sizeof(int));
     cand = o; o = align256(o + (size_t)bs * nchunk * NB * sizeof(int));
@@ -301,6 +301,7 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
   A.perm = reinterpret_cast<int*>(w + Lw.perm);
   A.flag = reinterpret_cast<int*>(w + Lw.flag);
   A.n = n;
+  A.grad = grad ? 1 : 0;
   A.primal = pf_grad ? 0 : 1;
   A.gscale = pf_grad ? typename Sc<T>::R(0.5) : typename Sc<T>::R(1);
   A.zsign = pf_grad ? J.sign : nullptr;
@@ -322,7 +323,7 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
       A.k0 = k0;
       A.kw = n - k0 < NB ? n - k0 : NB;
       A.nchunk = (n - k0 + kLgChunk - 1) / kLgChunk;
-      lg_leaf_kernel<T><<<dim3(A.nchunk, cnt), kLgChunk, leaf_smem, s>>>(A);
+      if (A.nchunk > 1) lg_leaf_kernel<T><<<dim3(A.nchunk, cnt), kLgChunk, leaf_smem, s>>>(A);
       lg_tree_kernel<T><<<cnt, kLgChunk, tree_smem, s>>>(A);
       const int c_lo = grad ? 0 : k0;
       lg_swap_kernel<T><<<dim3((n - c_lo + 255) / 256, cnt), 256, 0, s>>>(A, c_lo);

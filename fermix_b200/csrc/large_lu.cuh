@@ -43,13 +43,14 @@ struct LgArgs {
   T* M;          // bs x n x n, the matrices being factorised (row-major)
   T* C;          // bs x n x NB coefficients of the current panel
   T* P;          // bs x NB x n snapshot of the current pivot rows
-  T* LU11;       // bs x 2 x NB x NB: L11 (strict lower), U11 (upper)
+  T* LU11;       // bs x 3 x NB x NB: L11 (strict lower), U11 (upper), A_PK^-1 (gradient)
   T* piv;        // bs x n pivots
   int* ipiv;     // bs x n interchanges (LAPACK order: row k swapped with ipiv[k])
   int* cand;     // bs x nchunk x NB leaf pivot rows
   int* perm;     // bs x n row permutation (gradient)
   int* flag;     // bs: non-finite entry seen in the inverse (gradient)
   int n, k0, kw, nchunk;
+  int grad;  // gradient mode (the tree kernel also forms A_PK^-1)
   // caller options: write (sign, logabs, value) (slogdet) or not (the Pfaffian gradient,
   // whose primal comes from the Parlett-Reid forward); scale of the gradient (1 for
   // slogdet, 1/2 for slogpf: d log pf / dS = S^-T / 2); zsign: a zero entry zeroes that
@@ -208,12 +209,18 @@ __global__ void __launch_bounds__(kLgChunk) lg_tree_kernel(LgArgs<T> A) {
   extern __shared__ __align__(16) unsigned char smem[];
   int* rows = reinterpret_cast<int*>(smem);  // [512] current pass
   int* sel = rows + kLgChunk;                // [NB] winners
-  int* allc = sel + NB;                      // [nchunk * NB] compacted candidates
-  int* ntot = allc + A.nchunk * NB;          // [1]
-  unsigned char* scratch = smem + (size_t)(kLgChunk + NB + A.nchunk * NB + 4) * sizeof(int);
+  const int nc = A.nchunk * NB > kLgChunk ? A.nchunk * NB : kLgChunk;
+  int* allc = sel + NB;                      // [nc] compacted candidates
+  int* ntot = allc + nc;                     // [1]
+  unsigned char* scratch = smem + (size_t)(kLgChunk + NB + nc + 4) * sizeof(int);
   const int b = blockIdx.x, n = A.n, kw = A.kw, k0 = A.k0;
   const int* cb = A.cand + (size_t)b * A.nchunk * NB;
-  if (threadIdx.x == 0) {
+  if (A.nchunk == 1) {
+    // one chunk (n - k0 <= 512): no leaf ran; every row of [k0, n) is a candidate and
+    // this pass is plain partial pivoting
+    for (int i = threadIdx.x; i < n - k0; i += blockDim.x) allc[i] = k0 + i;
+    if (threadIdx.x == 0) *ntot = n - k0;
+  } else if (threadIdx.x == 0) {
     int m = 0;
     for (int i = 0; i < A.nchunk * kw; ++i) {
       const int r = cb[(i / kw) * NB + i % kw];
@@ -237,8 +244,36 @@ __global__ void __launch_bounds__(kLgChunk) lg_tree_kernel(LgArgs<T> A) {
     consumed += more;
   }
   __syncthreads();
-  T* LU = A.LU11 + (size_t)b * 2 * NB * NB;
+  T* LU = A.LU11 + (size_t)b * 3 * NB * NB;
   lg_gepp<T, NB>(Mb, n, k0, kw, rows, count, sel, LU, LU + NB * NB, A.piv + (size_t)b * n + k0, true, scratch);
+  if (A.grad && threadIdx.x < kw) {
+    // row j of A_PK^-1 = (e_j U11^-1) L11^-1, one thread per row (the gradient's
+    // coefficients of the pivot rows and of the rows above the panel)
+    const T* L = LU;
+    const T* U = LU + NB * NB;
+    const int j = threadIdx.x;
+    T w[NB], c[NB];
+#pragma unroll
+    for (int t = 0; t < NB; ++t) {
+      T acc = (t == j) ? s_one<T>() : s_zero<T>();
+#pragma unroll
+      for (int q = 0; q < NB; ++q)
+        if (q < t) acc = fms(acc, w[q], U[q * NB + t]);
+      const T d = U[t * NB + t];
+      w[t] = (t < kw && t >= j && !is_zero(d)) ? sdiv(acc, d) : s_zero<T>();
+    }
+#pragma unroll
+    for (int t = NB - 1; t >= 0; --t) {
+      T acc = w[t];
+#pragma unroll
+      for (int q = 0; q < NB; ++q)
+        if (q > t && q < kw) acc = fms(acc, c[q], L[q * NB + t]);
+      c[t] = t < kw ? acc : s_zero<T>();
+    }
+    T* Ai = LU + 2 * NB * NB + j * NB;
+#pragma unroll
+    for (int t = 0; t < NB; ++t) Ai[t] = c[t];
+  }
   if (threadIdx.x == 0) {
     // positions of the chosen rows as earlier interchanges move them
     int cur[NB];
@@ -253,9 +288,11 @@ __global__ void __launch_bounds__(kLgChunk) lg_tree_kernel(LgArgs<T> A) {
   }
 }
 
+// allc holds max(nchunk * NB, 512) candidates (all rows of a single chunk)
 template <typename T>
 inline size_t lg_tree_smem(int nchunk) {
-  return (size_t)(kLgChunk + LgCfg<T>::NB + nchunk * LgCfg<T>::NB + 4) * sizeof(int) + lg_gepp_smem<T>();
+  const int nc = nchunk * LgCfg<T>::NB > kLgChunk ? nchunk * LgCfg<T>::NB : kLgChunk;
+  return (size_t)(kLgChunk + LgCfg<T>::NB + nc + 4) * sizeof(int) + lg_gepp_smem<T>();
 }
 
 // 3. interchanges on the columns [c_lo, n) of the whole rows, then the pivot-row snapshot
@@ -283,12 +320,13 @@ __global__ void __launch_bounds__(256) lg_swap_kernel(LgArgs<T> A, int c_lo) {
 template <typename T, bool GRAD>
 __global__ void __launch_bounds__(256) lg_coef_kernel(LgArgs<T> A, int r_lo) {
   constexpr int NB = LgCfg<T>::NB;
-  __shared__ T sL[NB * NB], sU[NB * NB];
+  __shared__ T sL[NB * NB], sU[NB * NB], sAi[GRAD ? NB * NB : 1];
   const int b = blockIdx.y, n = A.n, k0 = A.k0, kw = A.kw;
-  const T* LU = A.LU11 + (size_t)b * 2 * NB * NB;
+  const T* LU = A.LU11 + (size_t)b * 3 * NB * NB;
   for (int i = threadIdx.x; i < NB * NB; i += blockDim.x) {
     sL[i] = LU[i];
     sU[i] = LU[NB * NB + i];
+    if (GRAD) sAi[i] = LU[2 * NB * NB + i];
   }
   __syncthreads();
   const int r = r_lo + blockIdx.x * blockDim.x + threadIdx.x;
@@ -298,32 +336,33 @@ __global__ void __launch_bounds__(256) lg_coef_kernel(LgArgs<T> A, int r_lo) {
   T c[NB];
   if (r >= k0 && r < k0 + kw) {
     if (!GRAD) return;
-    // pivot row j: w = e_j U11^-1, then c = w L11^-1 (row j of A_PK^-1)
+    // pivot row j: the exchanged block gets row j of A_PK^-1, the coefficient e_j + it
     const int j = r - k0;
-    T w[NB];
+#pragma unroll
+    for (int t = 0; t < NB; ++t) c[t] = t < kw ? sAi[j * NB + t] : s_zero<T>();
+#pragma unroll
+    for (int t = 0; t < NB; ++t)
+      if (t < kw) row[t] = c[t];
+#pragma unroll
+    for (int t = 0; t < NB; ++t)
+      if (t == j) c[t] = add(c[t], s_one<T>());
+  } else if (GRAD && r < k0) {
+    // a row above the panel (already exchanged): C = M_xK A_PK^-1, a plain product (these
+    // rows never feed the pivots)
+    T a[NB];
+#pragma unroll
+    for (int q = 0; q < NB; ++q) a[q] = q < kw ? row[q] : s_zero<T>();
 #pragma unroll
     for (int t = 0; t < NB; ++t) {
-      T acc = (t == j) ? s_one<T>() : s_zero<T>();
+      T acc = s_zero<T>();
 #pragma unroll
       for (int q = 0; q < NB; ++q)
-        if (q < t) acc = fms(acc, w[q], sU[q * NB + t]);
-      const T d = sU[t * NB + t];
-      w[t] = (t < kw && t >= j && !is_zero(d)) ? sdiv(acc, d) : s_zero<T>();
-    }
-#pragma unroll
-    for (int t = NB - 1; t >= 0; --t) {
-      T acc = w[t];
-#pragma unroll
-      for (int q = 0; q < NB; ++q)
-        if (q > t && q < kw) acc = fms(acc, c[q], sL[q * NB + t]);
+        if (q < kw) acc = fma_(a[q], sAi[q * NB + t], acc);
       c[t] = t < kw ? acc : s_zero<T>();
     }
 #pragma unroll
     for (int t = 0; t < NB; ++t)
-      if (t < kw) row[t] = c[t];  // the exchanged block: A_PK^-1
-#pragma unroll
-    for (int t = 0; t < NB; ++t)
-      if (t == j) c[t] = add(c[t], s_one<T>());
+      if (t < kw) row[t] = c[t];
   } else {
     // l = M_xK U11^-1 (the elimination's FMA chains), then C L11 = l
     T l[NB];
