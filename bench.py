@@ -124,16 +124,16 @@ def peaks():
 
 
 def traffic_from_profiles(a):
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary
-    (a line 'traffic_bytes_per_launch: X' for this workload), else None."""
+    """DRAM bytes per launch of the dominant kernel: the committed ncu summary's line
+    'traffic_bytes_per_matrix: X' for this workload, times the batch; else None."""
     name = f"{kernel_name(a)}_{a.dtype}_n{a.n}_{'fwd' if a.fwd_only else 'fwdbwd'}.md"
     p = os.path.join(ROOT, "profiles", name)
-    if not os.path.exists(p):
+    if a.gather or not os.path.exists(p):
         return None
     for line in open(p):
-        if line.strip().startswith("traffic_bytes_per_launch_scaled:"):
+        if line.strip().startswith("traffic_bytes_per_matrix:"):
             try:
-                return float(line.split(":", 1)[1].strip().split()[0])
+                return float(line.split(":", 1)[1].strip().split()[0]) * a.batch
             except ValueError:
                 return None
     return None
