@@ -246,33 +246,51 @@ __global__ void __launch_bounds__(kLgChunk) lg_tree_kernel(LgArgs<T> A) {
   __syncthreads();
   T* LU = A.LU11 + (size_t)b * 3 * NB * NB;
   lg_gepp<T, NB>(Mb, n, k0, kw, rows, count, sel, LU, LU + NB * NB, A.piv + (size_t)b * n + k0, true, scratch);
-  if (A.grad && threadIdx.x < kw) {
-    // row j of A_PK^-1 = (e_j U11^-1) L11^-1, one thread per row (the gradient's
-    // coefficients of the pivot rows and of the rows above the panel)
+  if (A.grad) {
+    // A_PK^-1 = U11^-1 L11^-1 for the gradient's pivot rows and swept rows: columns of
+    // L11^-1 (threads 0 .. kw-1) and rows of U11^-1 (threads 32 .. 32 + kw-1) in parallel,
+    // then the product, two entries per thread
+    __syncthreads();  // L11 / U11 written by lg_gepp
+    T* Li = reinterpret_cast<T*>(scratch);  // [NB][NB] L11^-1, then reused
+    T* Ui = Li + NB * NB;                   // [NB][NB] U11^-1
     const T* L = LU;
     const T* U = LU + NB * NB;
-    const int j = threadIdx.x;
-    T w[NB], c[NB];
+    const int tid = threadIdx.x;
+    if (tid < kw) {
+      const int t = tid;  // column t of L11^-1: unit lower forward substitution
+      T y[NB];
 #pragma unroll
-    for (int t = 0; t < NB; ++t) {
-      T acc = (t == j) ? s_one<T>() : s_zero<T>();
+      for (int r = 0; r < NB; ++r) {
+        T acc = (r == t) ? s_one<T>() : s_zero<T>();
 #pragma unroll
-      for (int q = 0; q < NB; ++q)
-        if (q < t) acc = fms(acc, w[q], U[q * NB + t]);
-      const T d = U[t * NB + t];
-      w[t] = (t < kw && t >= j && !is_zero(d)) ? sdiv(acc, d) : s_zero<T>();
+        for (int q = 0; q < NB; ++q)
+          if (q < r) acc = fms(acc, L[r * NB + q], y[q]);
+        y[r] = (r >= t && r < kw) ? acc : s_zero<T>();
+        Li[r * NB + t] = y[r];
+      }
+    } else if (tid >= 32 && tid < 32 + kw) {
+      const int j = tid - 32;  // row j of U11^-1: w U11 = e_j
+      T w[NB];
+#pragma unroll
+      for (int t = 0; t < NB; ++t) {
+        T acc = (t == j) ? s_one<T>() : s_zero<T>();
+#pragma unroll
+        for (int q = 0; q < NB; ++q)
+          if (q < t) acc = fms(acc, w[q], U[q * NB + t]);
+        const T d = U[t * NB + t];
+        w[t] = (t < kw && t >= j && !is_zero(d)) ? sdiv(acc, d) : s_zero<T>();
+        Ui[j * NB + t] = w[t];
+      }
     }
-#pragma unroll
-    for (int t = NB - 1; t >= 0; --t) {
-      T acc = w[t];
-#pragma unroll
-      for (int q = 0; q < NB; ++q)
-        if (q > t && q < kw) acc = fms(acc, c[q], L[q * NB + t]);
-      c[t] = t < kw ? acc : s_zero<T>();
+    __syncthreads();
+    T* Ai = LU + 2 * NB * NB;
+    for (int e = tid; e < NB * NB; e += blockDim.x) {
+      const int j = e / NB, t = e % NB;
+      T acc = s_zero<T>();
+      if (j < kw && t < kw)
+        for (int r = 0; r < kw; ++r) acc = fma_(Ui[j * NB + r], Li[r * NB + t], acc);
+      Ai[e] = acc;
     }
-    T* Ai = LU + 2 * NB * NB + j * NB;
-#pragma unroll
-    for (int t = 0; t < NB; ++t) Ai[t] = c[t];
   }
   if (threadIdx.x == 0) {
     // positions of the chosen rows as earlier interchanges move them
@@ -288,11 +306,15 @@ __global__ void __launch_bounds__(kLgChunk) lg_tree_kernel(LgArgs<T> A) {
   }
 }
 
-// allc holds max(nchunk * NB, 512) candidates (all rows of a single chunk)
+// allc holds max(nchunk * NB, 512) candidates (all rows of a single chunk); the scratch
+// behind it serves lg_gepp, then L11^-1 and U11^-1 (2 NB^2 entries) in gradient mode
 template <typename T>
 inline size_t lg_tree_smem(int nchunk) {
-  const int nc = nchunk * LgCfg<T>::NB > kLgChunk ? nchunk * LgCfg<T>::NB : kLgChunk;
-  return (size_t)(kLgChunk + LgCfg<T>::NB + nc + 4) * sizeof(int) + lg_gepp_smem<T>();
+  constexpr int NB = LgCfg<T>::NB;
+  const int nc = nchunk * NB > kLgChunk ? nchunk * NB : kLgChunk;
+  const size_t inv = 2 * (size_t)NB * NB * sizeof(T);
+  const size_t scratch = lg_gepp_smem<T>() > inv ? lg_gepp_smem<T>() : inv;
+  return (size_t)(kLgChunk + NB + nc + 4) * sizeof(int) + scratch;
 }
 
 // 3. interchanges on the columns [c_lo, n) of the whole rows, then the pivot-row snapshot
