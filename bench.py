@@ -115,6 +115,42 @@ def compute_roofline(a, flops_per_launch, launch_s):
     return {"pipe": pipe, "achieved_tflops": achieved, "peak_tflops": peak, "frac": achieved / peak}
 
 
+def launches_per_call(a, sms=148):
+    """Kernels one library call launches for this workload, mirroring the dispatch of
+    fermix_b200/csrc/api.cu: one for n <= 256 (odd-n slogpf, the closed forms, the
+    tensor-memory and register-panel kernels); for n > 256 the blocked engines' kernels per
+    panel and per batch slice (a slice: at most SMs x 4 matrices and about 8 GiB)."""
+    n, B = a.n, a.batch
+    if n <= 256 or (a.op == "slogpf" and n % 2):
+        return 1
+    s = {"f32": 4, "f64": 8, "c64": 8, "c128": 16}[a.dtype]
+    nb = 32 if s <= 8 else 16
+    per_mat = n * n * s + 2 * n * nb * s + 3 * nb * nb * s + n * s + 3 * n * 4 + ((n + 511) // 512) * nb * 4
+    bs = max(1, min(B, sms * 4, (8 << 30) // per_mat))
+    slices = (B + bs - 1) // bs
+    grad = not a.fwd_only
+
+    def lu_engine():
+        k = 0
+        for k0 in range(0, n, nb):
+            kw = min(nb, n - k0)
+            k += (1 if (n - k0 + 511) // 512 > 1 else 0) + 3 + (1 if (grad or k0 + kw < n) else 0)
+        return k + 1 + (2 if grad else 0)
+
+    if a.op == "slogdet":
+        return slices * lu_engine()
+    # slogpf: the skew copy, per panel the panel kernel, two swaps and the update, the finish
+    npair = (nb // 2) if n <= 512 else (8 if s <= 8 else 4)
+    k = 1
+    for k0 in range(0, n, 2 * npair):
+        np_ = min(npair, (n - k0) // 2)
+        k += 3 + (1 if k0 + 2 * np_ < n else 0)
+    k += 1
+    if grad:
+        k += 1 + lu_engine()  # the skew copy of the gradient engine, then the LU engine
+    return slices * k
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -347,6 +383,33 @@ def main():
                                            logabs.data_ptr(), None, Gout.data_ptr(), ws.data_ptr(), wsb)
         _lib.check(st)
 
+    def call_chunk(b0, cnt, X, Gout, strm):
+        """One C-ABI call on matrices [b0, b0 + cnt) of X / Gout (the e2e pipeline's
+        chunks), on stream strm."""
+        es = X.element_size()
+        off = b0 * n * n * es
+        sgn_p = sign.data_ptr() + b0 * sign.element_size()
+        la_p = logabs.data_ptr() + b0 * logabs.element_size()
+        g_p = None if Gout is None else Gout.data_ptr() + off
+        x_p = X.data_ptr() + off
+        wsc = L.fermix_workspace_bytes(op, kind, cnt, n, 0 if a.fwd_only else 1)
+        wsp = wsc_buf[strm].data_ptr() if wsc else None
+        if a.op == "slogpf":
+            if a.fwd_only:
+                st = L.fermix_slogpf(strm, kind, prec, cnt, n, 1, x_p, sgn_p, la_p, None, wsp, wsc)
+            else:
+                st = L.fermix_slogpf_grad(strm, kind, prec, cnt, n, 1, x_p, None, 0, 0, sgn_p, la_p, None, g_p, wsp,
+                                          wsc)
+        else:
+            if a.fwd_only:
+                st = L.fermix_slogdet(strm, kind, prec, cnt, n, x_p, sgn_p, la_p, None, wsp, wsc)
+            else:
+                st = L.fermix_slogdet_grad(strm, kind, prec, cnt, n, x_p, None, 0, 0, sgn_p, la_p, None, g_p, wsp,
+                                           wsc)
+        _lib.check(st)
+
+    wsc_buf = {}
+
     def barrier():
         if dist is not None:
             dist.barrier()
@@ -425,16 +488,48 @@ def main():
             hP = torch.empty(PHI.shape, dtype=tdt, pin_memory=True)
             hP.copy_(PHI)
         ke = max(3, min(a.steps, 20))
+        # the step in CH chunks on three streams (copy in, compute, copy out), so that the
+        # two copy directions and the compute overlap; every call goes through the C ABI
+        CH = 1 if a.gather else 8
+        s_in, s_cmp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+        bounds = [(B * c // CH, B * (c + 1) // CH) for c in range(CH)]
+        if not a.gather:
+            wmax = L.fermix_workspace_bytes(op, kind, max(e - b for b, e in bounds), n, 0 if a.fwd_only else 1)
+            wsc_buf[s_cmp.cuda_stream] = torch.empty(max(wmax, 1), dtype=torch.uint8, device=dev)
 
         def e2e_step():
-            if hP is not None:
-                PHI.copy_(hP, non_blocking=True)
-            dA.copy_(hA, non_blocking=True)
-            call(dA, dG)
-            hS.copy_(sign, non_blocking=True)
-            hL.copy_(logabs, non_blocking=True)
-            if hG is not None:
-                hG.copy_(dG, non_blocking=True)
+            if a.gather:
+                if hP is not None:
+                    PHI.copy_(hP, non_blocking=True)
+                dA.copy_(hA, non_blocking=True)
+                call(dA, dG)
+                hS.copy_(sign, non_blocking=True)
+                hL.copy_(logabs, non_blocking=True)
+                if hG is not None:
+                    hG.copy_(dG, non_blocking=True)
+                return
+            start = torch.cuda.Event()
+            start.record(stream)
+            for s_ in (s_in, s_cmp, s_out):
+                s_.wait_event(start)
+            for b0, b1 in bounds:
+                with torch.cuda.stream(s_in):
+                    dA[b0:b1].copy_(hA[b0:b1], non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(s_in)
+                s_cmp.wait_event(ev_in)
+                call_chunk(b0, b1 - b0, dA, dG, s_cmp.cuda_stream)
+                ev_c = torch.cuda.Event()
+                ev_c.record(s_cmp)
+                s_out.wait_event(ev_c)
+                with torch.cuda.stream(s_out):
+                    hS[b0:b1].copy_(sign[b0:b1], non_blocking=True)
+                    hL[b0:b1].copy_(logabs[b0:b1], non_blocking=True)
+                    if hG is not None:
+                        hG[b0:b1].copy_(dG[b0:b1], non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(s_out)
+            stream.wait_event(done)
 
         for _ in range(2):
             e2e_step()
@@ -492,7 +587,7 @@ def main():
             "compute_roofline": compute_roofline(a, B * fl, launch_s),
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": a.steps,
+            "gpu_launches": a.steps * launches_per_call(a),
             "clocks": ck,
         }
         print(json.dumps(line), flush=True)

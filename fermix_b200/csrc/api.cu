@@ -419,9 +419,16 @@ int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
       } else if (m <= kPflRows) {
         pfl_panel_kernel<T, NP, kPflRows><<<cnt, kPflRows, psmem, s>>>(A);
       } else {
-        const int cl = (m + kPflRows - 1) / kPflRows;
-        const int e = cl == 2 ? launch_pfl_cl<T, 2>(s, A, cnt)
-                              : (cl == 3 ? launch_pfl_cl<T, 3>(s, A, cnt) : launch_pfl_cl<T, 4>(s, A, cnt));
+        int e = FX_ERR_SHAPE;
+        switch ((m + kPflRows - 1) / kPflRows) {
+          case 2: e = launch_pfl_cl<T, 2>(s, A, cnt); break;
+          case 3: e = launch_pfl_cl<T, 3>(s, A, cnt); break;
+          case 4: e = launch_pfl_cl<T, 4>(s, A, cnt); break;
+          case 5: e = launch_pfl_cl<T, 5>(s, A, cnt); break;
+          case 6: e = launch_pfl_cl<T, 6>(s, A, cnt); break;
+          case 7: e = launch_pfl_cl<T, 7>(s, A, cnt); break;
+          case 8: e = launch_pfl_cl<T, 8>(s, A, cnt); break;
+        }
         if (e) return e;
       }
       pfl_swap_rows_kernel<T><<<dim3((n - k0 + 255) / 256, cnt), 256, 0, s>>>(A);

@@ -1,4 +1,4 @@
-// Blocked Parlett-Reid engine for the slogpf forward at 256 < n <= 1024, every dtype: a
+// Blocked Parlett-Reid engine for the slogpf forward at 256 < n <= 8192, every dtype: a
 // host-driven loop over panels of NP pairs, each panel three batched kernels, the
 // matrices in the caller's workspace (skew-symmetrised copies).
 //
@@ -190,12 +190,12 @@ inline size_t pfl_panel_smem() {
 }
 
 // ---------------------------------------------------------------- cluster panel
-// 1024 < n - k0 <= 4096: the panel's rows split over a cluster of CL blocks (1024 rows
-// each). Every block keeps its rows' pair factors and a full copy of the position
+// 1024 < n - k0 <= 8192: the panel's rows split over a cluster of CL <= 8 blocks (1024
+// rows each; 8 is the portable cluster size). Every block keeps its rows' pair factors and a full copy of the position
 // bookkeeping; the pivot search combines the blocks' candidates through distributed
 // shared memory, and the pivot rows' factors are read from the block that owns them. Two
 // cluster barriers per pair step, executed by every thread of every block.
-constexpr int kPflMaxN = 4 * kPflRows;
+constexpr int kPflMaxN = 8 * kPflRows;
 
 __device__ __forceinline__ uint32_t cl_rank() {
   uint32_t r;

@@ -464,3 +464,22 @@ def test_n300_det_adjugate_primal_matches_forward(dtype):
     s64, l64 = np.linalg.slogdet(ref64(A))
     want = np.swapaxes(np.linalg.inv(ref64(A)), -1, -2) * (s64 * np.exp(l64))[:, None, None]
     assert relerr(g, want) < tol(dtype, 1e-3, 1e-9)
+
+
+def test_cluster_panel_pfaffian_known_value():
+    """n = 4200 > 4096: the large-n Parlett-Reid panel spans a cluster of five blocks at
+    first. S = Q J Q^T with J = diag([[0, 1], [-1, 0]]) and Q = D L (D diagonal, L unit
+    lower) has pf(S) = det(Q) = prod(D)."""
+    n = 4200
+    gen = np.random.default_rng(43)
+    d = gen.uniform(0.7, 1.4, n) * gen.choice([-1.0, 1.0], n)
+    Lw = np.tril(gen.standard_normal((n, n)) * (0.3 / np.sqrt(n)), -1) + np.eye(n)
+    Q = d[:, None] * Lw
+    J = np.kron(np.eye(n // 2), np.array([[0.0, 1.0], [-1.0, 0.0]]))
+    M = Q @ J @ Q.T
+    S = 0.5 * (M - M.T)
+    s, l = host(fx.slogpf(cuda(S[None])))
+    want_s = np.prod(np.sign(d))
+    want_l = np.sum(np.log(np.abs(d)))
+    assert s[0] == want_s
+    assert abs(l[0] - want_l) < 1e-8 * max(1.0, abs(want_l))
