@@ -153,7 +153,7 @@ int launch_pf_tc(cudaStream_t s, Job<float> J) {
 // one 256-thread block per SM holding the whole matrix in the SM's 512 TMEM columns, its
 // shared-memory request above half the SM so that no second block (a tcgen05.alloc
 // waiter) is placed beside it.
-constexpr size_t kLuTcSmem = 55 * 1024;  // at most four blocks per SM (4 x 56 KB)
+constexpr size_t kLuTcSmem = 56 * 1024;  // four blocks per SM: 4 x (56 KB + 1 KB reserved) = 228 KB
 static_assert(sizeof(LuTcSmemT<128>) <= kLuTcSmem, "LuTcSmem too large");
 constexpr size_t kLuTc256Smem = 120 * 1024;
 static_assert(sizeof(LuTcSmemT<256>) <= kLuTc256Smem, "LuTcSmemT<256> too large");

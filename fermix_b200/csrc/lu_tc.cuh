@@ -50,6 +50,7 @@ struct LuTcSmemT {
   float U11[16][17];                                // the pivot rows' panel entries (upper part)
   float Linv[16][17];                               // L11^-1 (gradient mode)
   float Uinv[16][17];                               // U11^-1 (gradient mode)
+  __align__(16) float Ainv[16][20];                 // A_PK^-1 = U11^-1 L11^-1 (gradient mode, 16-byte rows)
   float dvec[NR];                                   // pivots
   int at[NR];                                       // pivot position -> row
   int wpar[NW];                                     // per-warp parity of the inversions
@@ -271,16 +272,32 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
       }
       FX_TOC(tq, 2);
       __syncthreads();  // prow, Linv, Uinv complete; the panel buffer is free
-      if (GRAD && inP) {
-        // row j of A_PK^-1 = U11^-1 L11^-1, then + e_j
-        const int j = mypos - k0;
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          float acc = t == j ? 1.f : 0.f;
+      if (GRAD) {
+        // A_PK^-1 = U11^-1 L11^-1 by the whole block (256 entries), then each pivot row
+        // reads its row and adds e_j
+        for (int e = tid; e < 256; e += NR) {
+          const int j = e >> 4, t = e & 15;
+          float acc = 0.f;
 #pragma unroll
           for (int r = 0; r < 16; ++r)
             if (r >= t && r < kw) acc = fmaf(S.Uinv[j][r], S.Linv[r][t], acc);
-          c[t] = t < kw ? acc : 0.f;
+          S.Ainv[j][t] = (j < kw && t < kw) ? acc : 0.f;
+        }
+        __syncthreads();
+        if (inP) {
+          const int j = mypos - k0;
+          const float4* r4 = reinterpret_cast<const float4*>(S.Ainv[j]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = r4[q];
+            c[4 * q] = v.x;
+            c[4 * q + 1] = v.y;
+            c[4 * q + 2] = v.z;
+            c[4 * q + 3] = v.w;
+          }
+#pragma unroll
+          for (int t = 0; t < 16; ++t)
+            if (t == j) c[t] += 1.f;
         }
       }
 #pragma unroll
