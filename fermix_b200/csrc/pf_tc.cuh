@@ -14,12 +14,20 @@
 // rank-16 block-sweep update D -= W B^T as six tcgen05.mma kind::tf32 instructions
 // (K = 16, hi / lo split) issued by one thread, accumulating in TMEM. In gradient mode the
 // panel's pivot rows and columns are then replaced by the block-sweep values
-//   A'_XP = A_XP A_PP^-1,  A'_PX = -+A'_XP^T,  A'_PP = -A_PP^-1,
+//   A'_XP = A_XP A_PP^-1,  A'_PY = sigma(y) A'_YP^T,  A'_PP = -A_PP^-1,
 // so that after the last panel TMEM holds -S^-1 (sweeping every index inverts the
 // matrix); the forward-only mode skips the replacement and its (sign, logabs) are
 // bit-identical (the unswept part evolves identically). Row-derived operand values come
-// from the column values by the sweep's sign pattern: skew inside the unswept and inside
-// the swept index sets, symmetric across them.
+// from the column values by the sweep's sign pattern sigma: skew inside the unswept and
+// inside the swept index sets, symmetric across them.
+//
+// The replacement needs no inverse of A_PP. The pair steps factor the panel as
+// A_XP = W_X B_P^T with B = sigma W D_J (D_J = diag of the pairs' [[0, -d], [d, 0]]) and
+// W_P (the pivot rows' multipliers) unit lower block-triangular, so
+//   A'_XP = W_X Z,  A_PP^-1 = Z^T D_J^-T Z,  Z = W_P^-1:
+// every thread solves z W_P = (its W row, or e_k on pivot row k) while the tensor core
+// runs the update, the pivot rows' new rows are the other rows' z transposed through
+// shared memory, and their pivot block is formed from the pivot rows' Z.
 #pragma once
 #include "fused_lu.cuh"
 #include "tc_common.cuh"
@@ -27,11 +35,15 @@
 namespace fx {
 
 struct PfTcSmem {
-  float u[8][kTcN];  // u_t[x] = col_p[x] / d_t of the panel's pairs (broadcast reads)
-  float v[8][kTcN];  // v_t[x] = -col_a[x] / d_t
+  // u_t[x] = col_p[x] / d_t, v_t[x] = -col_a[x] / d_t of the panel's pairs (broadcast reads);
+  // in gradient mode both are reused after the pair steps as tcol[16][kTcN], the other rows'
+  // new pivot-column values sigma(x) z_j(x) read back along the pivot rows
+  __align__(16) float u[8][kTcN];
+  float v[8][kTcN];
   float whi[kTcN * 16], wlo[kTcN * 16];  // MMA A operand (K-major, interleaved), TF32 hi / lo
   float bhi[kTcN * 16], blo[kTcN * 16];  // MMA B operand
-  __align__(16) float app[16][20];       // A_PP of the panel, then A_PP^-1 (16-byte rows)
+  __align__(16) float wp[16][20];        // W_P: the pivot rows' multipliers (16-byte rows)
+  __align__(16) float zp[16][20];        // Z = W_P^-1, row k from pivot row k
   uint4 pcand[4];                        // per-warp pivot candidates: key, row, -, value bits
   int cand_f[4];                         // scratch (the singular flag at the end)
   int at[kTcN], pof[kTcN];               // position -> row, row -> position (virtual pivoting)
@@ -39,61 +51,13 @@ struct PfTcSmem {
   unsigned char isP[kTcN];
   float dvec[kTcN / 2];
   uint32_t tslot;
-  uint32_t dis[4];  // MMA output-lane mask: lanes that are not pivot rows
   int parity, bad;
   uint64_t mbar;
 };
-
-// Inverse of the m x m (m = 2 np <= 16) pivot block in S.app by sequential 2 x 2 pair
-// sweeps (pairs (2q, 2q+1)); warp 0, lane k owns row k. Result: S.app = A_PP^-1.
-__device__ void tc_block_inverse(PfTcSmem& S, int np) {
-  const int lane = threadIdx.x & 31;
-  const int m = 2 * np;
-  float r[16];
-#pragma unroll
-  for (int y = 0; y < 16; ++y) r[y] = (lane < m && y < m) ? S.app[lane][y] : 0.f;
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    if (q < np) {
-      const int i = 2 * q, j = i + 1;
-      float ri[16], rj[16];
-#pragma unroll
-      for (int y = 0; y < 16; ++y) {
-        ri[y] = __shfl_sync(0xffffffffu, r[y], i);
-        rj[y] = __shfl_sync(0xffffffffu, r[y], j);
-      }
-      const float d00 = ri[i], d01 = ri[j], d10 = rj[i], d11 = rj[j];
-      const float det = d00 * d11 - d01 * d10;
-      const float id = det == 0.f ? 0.f : __fdiv_rn(1.f, det);
-      const float e00 = d11 * id, e01 = -d01 * id, e10 = -d10 * id, e11 = d00 * id;
-      if (lane == i || lane == j) {
-        const float f0 = lane == i ? e00 : e10, f1 = lane == i ? e01 : e11;
-#pragma unroll
-        for (int y = 0; y < 16; ++y)
-          if (y != i && y != j) r[y] = fmaf(f0, ri[y], f1 * rj[y]);
-        r[i] = -f0;
-        r[j] = -f1;
-      } else if (lane < m) {
-        const float xi = r[i], xj = r[j];
-        const float ci = fmaf(xi, e00, xj * e10), cj = fmaf(xi, e01, xj * e11);
-#pragma unroll
-        for (int y = 0; y < 16; ++y)
-          if (y != i && y != j) r[y] = fmaf(-ci, ri[y], fmaf(-cj, rj[y], r[y]));
-        r[i] = ci;
-        r[j] = cj;
-      }
-    }
-  }
-  __syncwarp();
-  if (lane < m) {
-#pragma unroll
-    for (int y = 0; y < 16; ++y)
-      if (y < m) S.app[lane][y] = -r[y];  // the sweep leaves -A_PP^-1
-  }
-}
+static_assert(offsetof(PfTcSmem, v) == offsetof(PfTcSmem, u) + sizeof(float) * 8 * kTcN, "u, v contiguous");
 
 template <bool GRAD>
-__global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
+__global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PfTcSmem& S = *reinterpret_cast<PfTcSmem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -137,11 +101,10 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
     for (int g0 = 0; g0 < npairs; g0 += 8) {
       const int np = min(8, npairs - g0);
       const bool swept_before = !live && x < n;
-      float ur[8], vr[8], dr[8], s0[16];
+      float ur[8], vr[8], dr[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         ur[t] = vr[t] = dr[t] = 0.f;
-        s0[2 * t] = s0[2 * t + 1] = 0.f;
       }
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
@@ -152,7 +115,6 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
           // column a of the current matrix: stale TMEM value plus this panel's corrections
           float colA = __uint_as_float(umma::tmem_ld1(trow + a));
           umma::tmem_wait_ld();
-          s0[2 * s] = colA;
 #pragma unroll
           for (int t = 0; t < 8; ++t)
             if (t < s) {
@@ -184,7 +146,6 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
           if (x == p) live = false;
           float colP = __uint_as_float(umma::tmem_ld1(trow + p));
           umma::tmem_wait_ld();
-          s0[2 * s + 1] = colP;
 #pragma unroll
           for (int t = 0; t < 8; ++t)
             if (t < s) {
@@ -217,20 +178,27 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
         }
       }
       FX_TOC(tq, 9);
-      // ---- gradient mode: the pivot block A_PP (rows of the pivot threads) for its inverse,
-      // and the output-lane mask of the pivot rows
+      // ---- gradient mode: pivot row k publishes its row of W_P, the multipliers of the
+      // earlier pairs (its own pair's identity block and the zero upper part are implied)
       int kx = -1;
       if (GRAD) {
 #pragma unroll
         for (int k = 0; k < 16; ++k)
           if (k < 2 * np && S.pidx[k] == x) kx = k;
         if (kx >= 0) {
+          const int kb = kx & ~1;
+          float4* w4 = reinterpret_cast<float4*>(S.wp[kx]);
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (j < 2 * np) S.app[kx][j] = s0[j];
+          for (int q = 0; q < 4; ++q) {
+            float e[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int j = 4 * q + c;
+              e[c] = j < kb ? ((j & 1) ? vr[j >> 1] : ur[j >> 1]) : 0.f;
+            }
+            w4[q] = make_float4(e[0], e[1], e[2], e[3]);
+          }
         }
-        const unsigned notP = __ballot_sync(0xffffffffu, kx < 0);
-        if (lane == 0) S.dis[warp] = notP;
       }
       // ---- MMA operands: W[x] = (u_t, v_t), B[x] = sigma(x) d_t (v_t, -u_t), 16-byte stores
       {
@@ -275,8 +243,70 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
         }
         umma::mma_commit(&S.mbar);
       }
-      // gradient mode: warp 0 inverts A_PP while the tensor core runs the update
-      if (GRAD && warp == 0) tc_block_inverse(S, np);
+      // gradient mode, while the tensor core runs the update: z W_P = rhs (rhs = this row's
+      // W, or e_kx on pivot row kx), from the last row of W_P up
+      float z[16], pp[16];
+      if (GRAD) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float wj = (j & 1) ? vr[j >> 1] : ur[j >> 1];
+          z[j] = kx >= 0 ? (j == kx ? 1.f : 0.f) : (j < 2 * np ? wj : 0.f);
+          pp[j] = 0.f;
+        }
+#pragma unroll
+        for (int m = 15; m >= 2; --m) {
+          if (m < 2 * np) {
+            const float zm = z[m];
+            const float4* r4 = reinterpret_cast<const float4*>(S.wp[m]);
+            const int mb = m & ~1;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (4 * q < mb) {
+                const float4 v = r4[q];
+                const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                  if (4 * q + c < mb) z[4 * q + c] = fmaf(-zm, vv[c], z[4 * q + c]);
+              }
+            }
+          }
+        }
+        // the other rows' new pivot-column values, transposed through shared memory for the
+        // pivot rows (A'_PY = sigma(y) A'_YP^T); pivot row kx keeps its row of Z
+        float* tcol = &S.u[0][0];
+        if (kx < 0) {
+          const float sg = swept_before ? -1.f : 1.f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < 2 * np) tcol[j * kTcN + x] = sg * z[j];
+        } else {
+          float4* z4 = reinterpret_cast<float4*>(S.zp[kx]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) z4[q] = make_float4(z[4 * q], z[4 * q + 1], z[4 * q + 2], z[4 * q + 3]);
+        }
+        __syncthreads();
+        // pivot row kx: A'_PP row = -(Z^T D_J^-T Z)[kx]
+        //   = sum_t (Z[2t][kx] Z[2t+1] - Z[2t+1][kx] Z[2t]) / d_t   (Z[j][kx] = 0 for j < kx)
+        if (kx >= 0) {
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            if (t < np && 2 * t + 1 >= kx) {
+              const float id = dr[t] == 0.f ? 0.f : __fdiv_rn(1.f, dr[t]);
+              const float za = S.zp[2 * t][kx] * id, zb = S.zp[2 * t + 1][kx] * id;
+              const float4* r0 = reinterpret_cast<const float4*>(S.zp[2 * t]);
+              const float4* r1 = reinterpret_cast<const float4*>(S.zp[2 * t + 1]);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 a = r0[q], c = r1[q];
+                pp[4 * q] = fmaf(za, c.x, fmaf(-zb, a.x, pp[4 * q]));
+                pp[4 * q + 1] = fmaf(za, c.y, fmaf(-zb, a.y, pp[4 * q + 1]));
+                pp[4 * q + 2] = fmaf(za, c.z, fmaf(-zb, a.z, pp[4 * q + 2]));
+                pp[4 * q + 3] = fmaf(za, c.w, fmaf(-zb, a.w, pp[4 * q + 3]));
+              }
+            }
+          }
+        }
+      }
       __syncwarp();
       if (!umma::mbar_wait(&S.mbar, phase, kTcWaitIters)) S.bad = 1;
       phase ^= 1;
@@ -284,91 +314,47 @@ __global__ void __launch_bounds__(128) pf_tc_kernel(Job<float> J) {
       FX_TOC(tq, 11);
 
       if (GRAD) {
-        // pivot rows / columns -> the block-sweep values (A = panel-start matrix):
-        //   A'_XP = A_XP A_PP^-1, A'_PP = -A_PP^-1 (16 TMEM column stores per thread),
-        //   A'_PY = A_PP^-1 A_PY = A_PP^-1 (tau(y) A_YP^T), tau = -1 unswept / +1 swept y,
-        // the latter as a second MMA whose output lanes are only the pivot rows.
-        __syncthreads();  // A_PP^-1 complete
-        FX_TOC(tq, 1);
-        float pv[16], a2[16];
+        // pivot rows: the whole row from the transposed values (a warp holding a pivot row
+        // stores all its lanes, the other lanes write back their own row)
+        if (__any_sync(0xffffffffu, kx >= 0)) {
+          const float* trow_src = &S.u[0][0] + (kx >= 0 ? kx : 0) * kTcN;
+#pragma unroll 1
+          for (int c0 = 0; c0 < kTcN; c0 += 32) {
+            uint32_t w[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) pv[j] = a2[j] = 0.f;
-        if (kx >= 0) {
-          const float4* r4 = reinterpret_cast<const float4*>(S.app[kx]);
+            for (int q = 0; q < 4; ++q) {
+              uint32_t t8[8];
+              umma::tmem_ld8(trow + c0 + 8 * q, t8);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 v = r4[q];
-            a2[4 * q] = v.x;
-            a2[4 * q + 1] = v.y;
-            a2[4 * q + 2] = v.z;
-            a2[4 * q + 3] = v.w;
-          }
+              for (int e = 0; e < 8; ++e) w[8 * q + e] = t8[e];
+            }
+            umma::tmem_wait_ld();
+            if (kx >= 0) {
+              const float4* s4 = reinterpret_cast<const float4*>(trow_src + c0);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) pv[j] = -a2[j];
-        } else {
-          // s0 A_PP^-1: broadcast 16-byte row loads, 16 independent accumulators
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            if (i < 2 * np) {
-              const float4* r4 = reinterpret_cast<const float4*>(S.app[i]);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float4 v = r4[q];
-                pv[4 * q] = fmaf(s0[i], v.x, pv[4 * q]);
-                pv[4 * q + 1] = fmaf(s0[i], v.y, pv[4 * q + 1]);
-                pv[4 * q + 2] = fmaf(s0[i], v.z, pv[4 * q + 2]);
-                pv[4 * q + 3] = fmaf(s0[i], v.w, pv[4 * q + 3]);
+              for (int q = 0; q < 8; ++q) {
+                const float4 v = s4[q];
+                w[4 * q] = __float_as_uint(v.x);
+                w[4 * q + 1] = __float_as_uint(v.y);
+                w[4 * q + 2] = __float_as_uint(v.z);
+                w[4 * q + 3] = __float_as_uint(v.w);
               }
             }
-          }
-        }
-        const float tau = swept_before ? 1.f : -1.f;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float ah[4], al[4], bh[4], bl[4];
+            for (int q = 0; q < 4; ++q) {
+              uint32_t t8[8];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = 4 * q + e;
-            const bool on = j < 2 * np;
-            if (!on) pv[j] = 0.f;
-            const float av = on ? a2[j] : 0.f, bv = on ? tau * s0[j] : 0.f;
-            ah[e] = umma::tf32_round(av);
-            al[e] = umma::tf32_round(av - ah[e]);
-            bh[e] = umma::tf32_round(bv);
-            bl[e] = umma::tf32_round(bv - bh[e]);
+              for (int e = 0; e < 8; ++e) t8[e] = w[8 * q + e];
+              umma::tmem_st8(trow + c0 + 8 * q, t8);
+            }
           }
-          const uint32_t off = umma::kmajor_offset(x, 4 * q, kTcSlab) / 4;
-          *reinterpret_cast<float4*>(&S.whi[off]) = make_float4(ah[0], ah[1], ah[2], ah[3]);
-          *reinterpret_cast<float4*>(&S.wlo[off]) = make_float4(al[0], al[1], al[2], al[3]);
-          *reinterpret_cast<float4*>(&S.bhi[off]) = make_float4(bh[0], bh[1], bh[2], bh[3]);
-          *reinterpret_cast<float4*>(&S.blo[off]) = make_float4(bl[0], bl[1], bl[2], bl[3]);
+          umma::tmem_wait_st();
         }
-        umma::fence_proxy_async_smem();
-        tc_sync();
-        FX_TOC(tq, 2);
-        if (tid == 0) {
-          const uint32_t idesc = umma::idesc_tf32(kTcN, kTcN, false);
-          const uint32_t dis[4] = {S.dis[0], S.dis[1], S.dis[2], S.dis[3]};
-#pragma unroll
-          for (int sl = 0; sl < 2; ++sl) {
-            const uint64_t ah = umma::smem_desc_kmajor(umma::smem_u32(S.whi) + sl * kTcSlab, 128, 256);
-            const uint64_t al = umma::smem_desc_kmajor(umma::smem_u32(S.wlo) + sl * kTcSlab, 128, 256);
-            const uint64_t bh = umma::smem_desc_kmajor(umma::smem_u32(S.bhi) + sl * kTcSlab, 128, 256);
-            const uint64_t bl = umma::smem_desc_kmajor(umma::smem_u32(S.blo) + sl * kTcSlab, 128, 256);
-            umma::mma_tf32_masked(tbase, ah, bh, idesc, sl > 0, dis);
-            umma::mma_tf32_masked(tbase, ah, bl, idesc, true, dis);
-            umma::mma_tf32_masked(tbase, al, bh, idesc, true, dis);
-          }
-          umma::mma_commit(&S.mbar);
-        }
-        __syncwarp();
-        if (!umma::mbar_wait(&S.mbar, phase, kTcWaitIters)) S.bad = 1;
-        phase ^= 1;
-        umma::fence_after_sync();
         FX_TOC(tq, 3);
+        // pivot columns of every row: A'_XP = z, on the pivot rows A'_PP = -A_PP^-1
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (j < 2 * np) umma::tmem_st1(trow + S.pidx[j], __float_as_uint(pv[j]));
+          if (j < 2 * np) umma::tmem_st1(trow + S.pidx[j], __float_as_uint(kx >= 0 ? pp[j] : z[j]));
         umma::tmem_wait_st();
         tc_sync();
         FX_TOC(tq, 4);
