@@ -64,6 +64,10 @@ def parse():
     ap.add_argument("--gather", type=int, default=0, metavar="SITES",
                     help="slogdet only: matrices are rows of a shared (SITES x n) phi picked by random occupations "
                          "(fermix_slogdet_gather, configuration 3's caller step); L2 flushed between timed steps")
+    ap.add_argument("--move", type=int, default=0, metavar="K",
+                    help="time a k-row move instead: fermix_slogdet_update (ratio + in-place Woodbury update of "
+                         "G = A^-T) on the batch; G stays resident, e2e copies only the new rows / indices in and the "
+                         "ratio out")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
@@ -301,6 +305,162 @@ def run_reference(a, rank):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------- k-row moves
+def run_move(a, rank, world, local):
+    """--move K: one step = one fermix_slogdet_update call (the ratio kernel, then the
+    in-place row update of every G = A^-T in the batch; every move accepted). HBM-bound:
+    the algorithmic bytes per matrix are one read and one write of G plus the k new rows."""
+    import numpy as np
+    import torch
+
+    from fermix_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    L = _lib.lib()
+    tdt = {"f32": torch.float32, "f64": torch.float64, "c64": torch.complex64, "c128": torch.complex128}[a.dtype]
+    rdt = torch.float32 if a.dtype in ("f32", "c64") else torch.float64
+    kind = {"f32": 0, "f64": 1, "c64": 2, "c128": 3}[a.dtype]
+    B, n, k = a.batch, a.n, a.move
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(a.seed + 1000 * rank)
+    # G of a well-conditioned A (identity-shifted); the moves replace random distinct rows by
+    # random rows near them, so every ratio stays O(1) while G is updated step after step
+    A = torch.randn((B, n, n), generator=gen, device=dev, dtype=tdt) / n**0.5 + 2 * torch.eye(n, device=dev)
+    G = torch.linalg.inv(A).transpose(-1, -2).contiguous()
+    IDX = torch.rand((B, n), generator=gen, device=dev).argsort(dim=1)[:, :k].to(torch.int32).contiguous()
+    U = (torch.gather(A, 1, IDX.long()[:, :, None].expand(B, k, n)) +
+         0.1 * torch.randn((B, k, n), generator=gen, device=dev, dtype=tdt) / n**0.5).contiguous()
+    del A
+    sign = torch.empty(B, dtype=tdt, device=dev)
+    logabs = torch.empty(B, dtype=rdt, device=dev)
+    wsb = L.fermix_slogdet_update_workspace_bytes(kind, B, n, k)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def call(Ud, Id):
+        _lib.check(L.fermix_slogdet_update(sp, kind, B, n, k, G.data_ptr(), Ud.data_ptr(), Id.data_ptr(), None,
+                                           sign.data_ptr(), logabs.data_ptr(), ws.data_ptr(), wsb))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(a.warmup):
+        call(U, IDX)
+    barrier()
+    clocks = Clocks(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                    os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+    clocks.start()
+    time.sleep(0.2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(a.steps):
+        call(U, IDX)
+    e1.record(stream)
+    barrier()
+    t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    ck = clocks.stop()
+    s = G.element_size()
+    by = 2 * n * n * s + k * n * s + k * 4  # G read + written, the new rows, the indices
+    launch_s = t_dev / a.steps  # both kernels of the call: an upper bound on the row kernel's time
+    hbm, peak_kind = peaks()
+    achieved = B * by / launch_s / 1e9
+    e2e = None
+    if not a.no_e2e:
+        hU = torch.empty(U.shape, dtype=tdt, pin_memory=True)
+        hU.copy_(U)
+        hI = torch.empty(IDX.shape, dtype=torch.int32, pin_memory=True)
+        hI.copy_(IDX)
+        dU, dI = torch.empty_like(U), torch.empty_like(IDX)
+        hS = torch.empty(B, dtype=tdt, pin_memory=True)
+        hL = torch.empty(B, dtype=rdt, pin_memory=True)
+        ke = max(3, min(a.steps, 50))
+
+        def e2e_step():
+            dU.copy_(hU, non_blocking=True)
+            dI.copy_(hI, non_blocking=True)
+            call(dU, dI)
+            hS.copy_(sign, non_blocking=True)
+            hL.copy_(logabs, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(ke):
+            e2e_step()
+        f1.record(stream)
+        barrier()
+        t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
+        e2e = {"value": world * B * ke / t_e2e, "unit": "moves/s",
+               "h2d_bytes_per_step": hU.numel() * hU.element_size() + hI.numel() * 4,
+               "d2h_bytes_per_step": hS.numel() * hS.element_size() + hL.numel() * hL.element_size(), "steps": ke}
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        from threadpoolctl import threadpool_limits
+
+        from oracle import moves
+
+        cnt = min(B, a.cpu_sample)
+        Gh, Uh, Ih = G[:cnt].cpu().numpy(), U[:cnt].cpu().numpy(), IDX[:cnt].cpu().numpy()
+        threads = os.cpu_count() or 1
+        with threadpool_limits(limits=threads):
+            t0 = time.perf_counter()
+            moves.ratio_woodbury(Gh, Uh, Ih)
+            moves.update_woodbury(Gh, Uh, Ih)
+            dt = time.perf_counter() - t0
+        cpu = {"value": cnt / dt, "unit": "moves/s", "cores": threads, "kind": "port",
+               "sample": f"{cnt} moves of the same workload ({dt:.2f} s; numpy Woodbury ratio + update in float64)"}
+    if rank == 0:
+        line = {
+            "metric": "k-row determinant moves/sec (ratio + in-place inverse update)",
+            "value": world * B * a.steps / t_dev,
+            "unit": "moves/s",
+            "n_gpus": world,
+            "steps": a.steps,
+            "warmup": a.warmup,
+            "ms_per_step": 1e3 * t_dev / a.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": a.dtype,
+            "data": "synthetic (seeded G = inv(A)^T of A ~ N(0, 1/n) + 2I, new rows near the replaced ones)",
+            "config": {"workload": f"slogdet {k}-row move {a.dtype} B={B}/GPU n={n}", "op": "slogdet_update",
+                       "batch_per_gpu": B, "n": n, "k": k, "parallelism": f"batch sharded x{world}, no collective",
+                       "l2": "G exceeds L2 (no flush needed)" if B * n * n * s > 126e6 else "G fits L2"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "kernel": "upd_rows_kernel", "algorithmic_bytes_per_launch": B * by},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": a.steps * 2,
+            "clocks": ck,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------- GPU arm
 def main():
     a = parse()
@@ -309,6 +469,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if a.impl == "reference":
         run_reference(a, rank)
+        return
+    if a.move:
+        run_move(a, rank, world, local)
         return
 
     import numpy as np

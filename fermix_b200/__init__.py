@@ -14,6 +14,8 @@ from .api import (
     pf_parts,
     slogdet,
     slogdet_gather,
+    slogdet_ratio,
+    slogdet_update,
     slogdet_parts,
     slogpf,
     slogpf_parts,
@@ -30,6 +32,8 @@ __all__ = [
     "det_parts",
     "pf_parts",
     "slogdet_gather",
+    "slogdet_ratio",
+    "slogdet_update",
     "FermixFallbackWarning",
     "__version__",
 ]

@@ -387,6 +387,82 @@ def slogdet_gather(phi, occ, *, prec=None):
     return sign.reshape(batch), logabs.reshape(batch)
 
 
+def _move_args(g, rows, idx):
+    """Checks of the rank-k move functions: g (..., n, n), rows (..., k, n), idx (..., k)."""
+    g = _prep(g)
+    n = g.shape[-1]
+    batch = tuple(g.shape[:-2])
+    rows = torch.as_tensor(rows, device=g.device)
+    if rows.dtype != g.dtype:
+        raise TypeError(f"rows must have the dtype of g ({g.dtype}), got {rows.dtype}")
+    if rows.dim() < 2 or rows.shape[-1] != n or tuple(rows.shape[:-2]) != batch:
+        raise ValueError(f"rows must have shape {batch + ('k', n)}, got {tuple(rows.shape)}")
+    k = rows.shape[-2]
+    if k > 16 or k > n:
+        raise ValueError(f"a move replaces at most min(16, n) rows, got k = {k}")
+    if not isinstance(idx, torch.Tensor):
+        idx = torch.as_tensor(np.asarray(idx))
+    if idx.dtype not in (torch.int32, torch.int64, torch.int16, torch.uint8):
+        raise TypeError("idx must be an integer tensor")
+    if tuple(idx.shape) != batch + (k,):
+        raise ValueError(f"idx must have shape {batch + (k,)}, got {tuple(idx.shape)}")
+    B = int(np.prod(batch)) if batch else 1
+    U = rows.detach().reshape(B, k, n).contiguous()
+    I = idx.to(device=g.device, dtype=torch.int32).reshape(B, k).contiguous()
+    return g, U, I, batch, B, n, k
+
+
+def slogdet_ratio(g, rows, idx):
+    """Determinant ratio of a k-row move (no reference counterpart: the single- and
+    multi-electron moves of a QMC caller). ``g`` (..., n, n) holds A^-T -- the gradient
+    ``slogdet_parts`` returns -- ``rows`` (..., k, n) the new rows and ``idx`` (..., k)
+    the distinct rows of A they replace, k <= min(16, n). Returns (sign, logabs) of
+    det(A') / det(A) = det(U A^-1 E) in the slogdet conventions; reads only k rows of each
+    g."""
+    g, U, I, batch, B, n, k = _move_args(g, rows, idx)
+    G = g.detach().reshape(B, n, n).contiguous()
+    sign = torch.empty(B, dtype=g.dtype, device=g.device)
+    logabs = torch.empty(B, dtype=_real(g.dtype), device=g.device)
+    with torch.cuda.device(g.device):
+        st = _lib.lib().fermix_slogdet_ratio(_stream_ptr(g.device), _KIND[g.dtype], B, n, k, _ptr(G), _ptr(U),
+                                             _ptr(I), _ptr(sign), _ptr(logabs))
+    _lib.check(st)
+    return sign.reshape(batch), logabs.reshape(batch)
+
+
+def slogdet_update(g, rows, idx, *, accept=None, inplace=False):
+    """Apply a k-row move to the inverse: as ``slogdet_ratio``, and also the new
+    A'^-T by the Woodbury identity for the members where ``accept`` (bool, shape
+    g.shape[:-2]; None = all) is true; the others keep g. A member whose ratio is exactly
+    0 gets a zero matrix (the slogdet gradient convention for a singular matrix). Returns
+    (sign, logabs, g_new); with ``inplace=True`` g (a contiguous CUDA tensor) is updated
+    and returned. Not differentiable."""
+    g, U, I, batch, B, n, k = _move_args(g, rows, idx)
+    if inplace:
+        if not g.is_contiguous():
+            raise ValueError("inplace=True needs a contiguous g")
+        G = g.detach().view(B, n, n)
+    else:
+        G = g.detach().reshape(B, n, n).clone()
+    acc = None
+    if accept is not None:
+        acc = torch.as_tensor(accept, device=g.device)
+        if tuple(acc.shape) != batch:
+            raise ValueError(f"accept must have shape {batch}, got {tuple(acc.shape)}")
+        acc = acc.to(torch.uint8).reshape(B).contiguous()
+    sign = torch.empty(B, dtype=g.dtype, device=g.device)
+    logabs = torch.empty(B, dtype=_real(g.dtype), device=g.device)
+    L = _lib.lib()
+    kind = _KIND[g.dtype]
+    with torch.cuda.device(g.device):
+        nbytes = L.fermix_slogdet_update_workspace_bytes(kind, B, n, k)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=g.device) if nbytes else None
+        st = L.fermix_slogdet_update(_stream_ptr(g.device), kind, B, n, k, _ptr(G), _ptr(U), _ptr(I), _ptr(acc),
+                                     _ptr(sign), _ptr(logabs), _ptr(ws), nbytes)
+    _lib.check(st)
+    return sign.reshape(batch), logabs.reshape(batch), (g if inplace else G.reshape(g.shape))
+
+
 def slogdet(a, *, prec=None, unroll_steps=None, block=None):
     """Sign and log|det| of a batch of matrices ``a`` of shape (..., n, n)
     (src/fermix/api.py:148-174). Returns (sign, logabsdet): sign has the dtype of ``a``

@@ -21,6 +21,7 @@
 #include "lu_tc.cuh"
 #include "large_lu.cuh"
 #include "large_pf.cuh"
+#include "update.cuh"
 
 namespace {
 
@@ -627,6 +628,55 @@ int run_gather(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* p
                     static_cast<unsigned char*>(ws) + mat, wsb - mat);
 }
 
+// ---------------------------------------------------------------- rank-k row updates
+// Workspace of fermix_slogdet_update: the per-matrix action (B ints), then H (B x k x n).
+template <typename T>
+size_t upd_ws_bytes(int64_t batch, int64_t n, int64_t k) {
+  return align256((size_t)batch * sizeof(int)) + align256((size_t)batch * k * n * sizeof(T));
+}
+
+int upd_validate(int dtype, int64_t batch, int64_t n, int64_t k) {
+  int e = validate(dtype, FX_PREC_DEFAULT, batch, n);
+  if (e) return e;
+  if (k < 0 || k > kUpdMaxK || k > n) return FX_ERR_SHAPE;
+  return FX_OK;
+}
+
+// ratio only (apply == false) or ratio plus the in-place update of G
+template <typename T>
+int run_update(cudaStream_t s, int64_t batch, int64_t n, int64_t k, void* g, const void* u, const int* idx,
+               const unsigned char* accept, void* sign, void* logabs, void* ws, size_t wsb, bool apply) {
+  const DevInfo* D = dev_info();
+  if (!D) return FX_ERR_DEVICE;
+  UpdArgs<T> A;
+  A.g = static_cast<T*>(g);
+  A.u = static_cast<const T*>(u);
+  A.idx = idx;
+  A.accept = accept;
+  A.sign = static_cast<T*>(sign);
+  A.logabs = static_cast<typename Sc<T>::R*>(logabs);
+  A.h = nullptr;
+  A.act = nullptr;
+  A.B = batch;
+  A.n = (int)n;
+  A.k = (int)k;
+  if (apply) {
+    if (!ws || wsb < upd_ws_bytes<T>(batch, n, k)) return FX_ERR_WORKSPACE;
+    A.act = static_cast<int*>(ws);
+    A.h = reinterpret_cast<T*>(static_cast<unsigned char*>(ws) + align256((size_t)batch * sizeof(int)));
+  }
+  const int64_t pcap = (int64_t)D->sms * 8;
+  upd_prep_kernel<T><<<(unsigned)(batch < pcap ? batch : pcap), kUpdPrepThreads, 0, s>>>(A);
+  if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  if (apply && k > 0) {
+    const int64_t wpb = kUpdRowThreads / 32;
+    const int64_t need = (batch * n + wpb - 1) / wpb, rcap = (int64_t)D->sms * 8;
+    upd_rows_kernel<T><<<(unsigned)(need < rcap ? need : rcap), kUpdRowThreads, 0, s>>>(A);
+    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  }
+  return FX_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -754,6 +804,42 @@ const char* fermix_strerror(int code) {
 }
 
 int fermix_version(void) { return 100; }
+
+int fermix_slogdet_ratio(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, const void* g,
+                         const void* rows, const int* idx, void* sign, void* logabs) {
+  int e = upd_validate(dtype, batch, n, k);
+  if (e) return e;
+  if (batch == 0) return FX_OK;
+  if ((k > 0 && (!g || !rows || !idx)) || !sign || !logabs) return FX_ERR_NULL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_update<T>(s, batch, n, k, const_cast<void*>(g), rows, idx, nullptr, sign, logabs, nullptr, 0,
+                         false);
+  });
+}
+
+int fermix_slogdet_update(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, void* g, const void* rows,
+                          const int* idx, const unsigned char* accept, void* sign, void* logabs, void* workspace,
+                          size_t workspace_bytes) {
+  int e = upd_validate(dtype, batch, n, k);
+  if (e) return e;
+  if (batch == 0) return FX_OK;
+  if ((k > 0 && (!g || !rows || !idx)) || !sign || !logabs) return FX_ERR_NULL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_update<T>(s, batch, n, k, g, rows, idx, accept, sign, logabs, workspace, workspace_bytes, true);
+  });
+}
+
+size_t fermix_slogdet_update_workspace_bytes(int dtype, int64_t batch, int64_t n, int64_t k) {
+  if (upd_validate(dtype, batch, n, k) || batch == 0) return 0;
+  return (size_t)by_dtype(dtype, [&](auto t) -> int {
+    using T = decltype(t);
+    return (int)((upd_ws_bytes<T>(batch, n, k) + 255) / 256);
+  }) * 256;
+}
 
 }  // extern "C"
 

@@ -1,0 +1,263 @@
+// Rank-k row replacement of determinants from the exported inverse (no reference
+// counterpart: the single- and multi-electron move of a QMC caller, built on the inverse
+// the gradient path exports -- _lu_parts, src/fermix/_inverse.py:502-531 -- and on the
+// reference's sign / logabs conventions for the ratio, src/fermix/_lu.py:614-621).
+//
+// State: G = A^-T, the slogdet gradient (fermix_slogdet_grad with coef = 1). A move
+// replaces rows idx[0 .. k) of A by the rows of U (k x n). With E = columns idx of I:
+//   R = U A^-1 E,  R[r][s] = U_r . G_{idx_s}           det(A') / det(A) = det(R)
+//   V = U A^-1,    V[r][j] = U_r . G_j
+//   G' = A'^-T = G - (V^T - E) H,  H = R^-T G[idx, :]   (Woodbury)
+// so row j of G' is G_j - sum_r (V[r][j] - [j == idx_r]) H_r.
+//
+// upd_prep_kernel: one 128-thread block per matrix. R by k^2 dot products (one warp each,
+//   fixed-order lane partials and an xor tree), its LU with partial pivoting by one thread
+//   (k <= 16, first-occurrence argmax of abs1 as the reference's LU) giving the ratio's
+//   (sign, logabs), then R^-1 and H into the workspace, and the matrix's row-kernel action.
+// upd_rows_kernel: one warp per row of G, in place: the k dot products V[.][j], then the row
+//   update. The row is read twice by the same warp (the second read hits L1 / L2); H and U
+//   are shared by all rows of a matrix and stay cache-resident, so HBM sees one read and
+//   one write of G: the kernel is HBM-bound at n^2 (read) + n^2 (write) elements.
+#pragma once
+#include "scalar.cuh"
+
+namespace fx {
+
+constexpr int kUpdMaxK = 16;  // largest rank of one move
+constexpr int kUpdPrepThreads = 128;
+constexpr int kUpdRowThreads = 256;
+
+enum : int { UPD_KEEP = 0, UPD_APPLY = 1, UPD_ZERO = 2 };
+
+template <typename T>
+struct UpdArgs {
+  T* g;                         // (B, n, n) G = A^-T; updated in place by the rows kernel
+  const T* u;                   // (B, k, n) replacement rows
+  const int* idx;               // (B, k) replaced row indices
+  const unsigned char* accept;  // (B,) apply the move where nonzero; null = every matrix
+  T* sign;                      // (B,) sign of det(A') / det(A) (input dtype)
+  typename Sc<T>::R* logabs;    // (B,) log |det(A') / det(A)|
+  T* h;                         // (B, k, n) workspace: H = R^-T G[idx, :]; null = ratio only
+  int* act;                     // (B,) workspace: UPD_KEEP / UPD_APPLY / UPD_ZERO
+  int64_t B;
+  int n, k;
+};
+
+template <typename T>
+__device__ __forceinline__ void upd_swap(T& a, T& b) {
+  const T t = a;
+  a = b;
+  b = t;
+}
+
+// NaN of the field (both parts for complex)
+template <typename T>
+__device__ __forceinline__ T upd_nan() {
+  using R = typename Sc<T>::R;
+  T v = s_zero<T>();
+  if constexpr (Sc<T>::cx) {
+    v.re = R(NAN);
+    v.im = R(NAN);
+  } else {
+    v = R(NAN);
+  }
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum_t(T v);
+template <>
+__device__ __forceinline__ float warp_sum_t<float>(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+template <>
+__device__ __forceinline__ double warp_sum_t<double>(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+template <>
+__device__ __forceinline__ c64_t warp_sum_t<c64_t>(c64_t v) {
+  return {warp_sum_t<float>(v.re), warp_sum_t<float>(v.im)};
+}
+template <>
+__device__ __forceinline__ c128_t warp_sum_t<c128_t>(c128_t v) {
+  return {warp_sum_t<double>(v.re), warp_sum_t<double>(v.im)};
+}
+
+// x . y over n entries: lane partials in column order, then the xor tree (every lane
+// returns the same bits; the rows kernel uses the same order, so V[r][idx_s] == R[r][s]).
+template <typename T>
+__device__ __forceinline__ T warp_dot(const T* __restrict__ x, const T* __restrict__ y, int n, int lane) {
+  T acc = s_zero<T>();
+  for (int c = lane; c < n; c += 32) acc = fma_(x[c], y[c], acc);
+  return warp_sum_t<T>(acc);
+}
+
+template <typename T>
+struct UpdSmem {
+  T r[kUpdMaxK][kUpdMaxK + 1];   // R, then its LU factors
+  T ri[kUpdMaxK][kUpdMaxK + 1];  // R^-1
+  int piv[kUpdMaxK];
+  int id[kUpdMaxK];
+  int bad, sing;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kUpdPrepThreads) upd_prep_kernel(UpdArgs<T> A) {
+  using R = typename Sc<T>::R;
+  __shared__ UpdSmem<T> S;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = A.n, k = A.k;
+  for (int64_t b = blockIdx.x; b < A.B; b += gridDim.x) {
+    const T* G = A.g + b * (int64_t)n * n;
+    const T* U = A.u + b * (int64_t)k * n;
+    if (tid == 0) S.bad = 0;
+    __syncthreads();
+    if (tid < k) {
+      const int v = A.idx[b * k + tid];
+      S.id[tid] = v;
+      if (v < 0 || v >= n) S.bad = 1;
+    }
+    __syncthreads();
+    const bool bad = S.bad != 0;
+    if (!bad) {
+      for (int p = warp; p < k * k; p += kUpdPrepThreads / 32) {
+        const int r = p / k, s = p - r * k;
+        const T v = warp_dot(U + (int64_t)r * n, G + (int64_t)S.id[s] * n, n, lane);
+        if (lane == 0) S.r[r][s] = v;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      // LU with partial pivoting of R: sign = prod unit(pivot) * (-1)^swaps,
+      // logabs = sum log|pivot| in column order; a zero pivot gives (0, -inf)
+      T sg = s_one<T>();
+      KSum<R> ls;
+      ls.init();
+      int sing = 0;
+      if (bad) {
+        sg = upd_nan<T>();
+      } else {
+        for (int c = 0; c < k; ++c) {
+          int p = c;
+          R best = abs1(S.r[c][c]);
+          for (int i = c + 1; i < k; ++i) {
+            const R m = abs1(S.r[i][c]);
+            if (m > best) {
+              best = m;
+              p = i;
+            }
+          }
+          S.piv[c] = p;
+          if (p != c) {
+            for (int j = 0; j < k; ++j) upd_swap(S.r[c][j], S.r[p][j]);
+            sg = neg(sg);
+          }
+          const T d = S.r[c][c];
+          if (is_zero(d)) {
+            sing = 1;
+            continue;
+          }
+          sg = mul(sg, unit(d));
+          ls.add(rlog(mag(d)));
+          const T dinv = recip(d);
+          for (int i = c + 1; i < k; ++i) {
+            const T l = mul(S.r[i][c], dinv);
+            S.r[i][c] = l;
+            for (int j = c + 1; j < k; ++j) S.r[i][j] = fms(S.r[i][j], l, S.r[c][j]);
+          }
+        }
+      }
+      R la = ls.value();
+      if (bad) la = R(NAN);
+      if (sing && !bad) {
+        sg = s_zero<T>();
+        la = -R(INFINITY);
+      }
+      A.sign[b] = sg;
+      A.logabs[b] = la;
+      S.sing = sing;
+      if (A.h) {
+        const bool acc = A.accept == nullptr || A.accept[b] != 0;
+        A.act[b] = (!acc || bad) ? UPD_KEEP : (sing ? UPD_ZERO : UPD_APPLY);
+        if (acc && !bad && !sing) {
+          // R^-1 column by column: P R = L U, solve L y = P e_c, then U x = y
+          for (int c = 0; c < k; ++c) {
+            T y[kUpdMaxK];
+            for (int i = 0; i < k; ++i) y[i] = (i == c) ? s_one<T>() : s_zero<T>();
+            for (int i = 0; i < k; ++i) {
+              const int p = S.piv[i];
+              if (p != i) upd_swap(y[i], y[p]);
+            }
+            for (int i = 0; i < k; ++i)
+              for (int j = 0; j < i; ++j) y[i] = fms(y[i], S.r[i][j], y[j]);
+            for (int i = k - 1; i >= 0; --i) {
+              for (int j = i + 1; j < k; ++j) y[i] = fms(y[i], S.r[i][j], y[j]);
+              y[i] = sdiv(y[i], S.r[i][i]);
+            }
+            for (int i = 0; i < k; ++i) S.ri[i][c] = y[i];
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (A.h && !bad && !S.sing && (A.accept == nullptr || A.accept[b] != 0)) {
+      // H[r][c] = sum_s R^-1[s][r] G[idx_s][c], coalesced over c
+      T* H = A.h + b * (int64_t)k * n;
+      for (int c = tid; c < n; c += kUpdPrepThreads) {
+        T gs[kUpdMaxK];
+        for (int s = 0; s < k; ++s) gs[s] = G[(int64_t)S.id[s] * n + c];
+        for (int r = 0; r < k; ++r) {
+          T acc = s_zero<T>();
+          for (int s = 0; s < k; ++s) acc = fma_(S.ri[s][r], gs[s], acc);
+          H[(int64_t)r * n + c] = acc;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kUpdRowThreads) upd_rows_kernel(UpdArgs<T> A) {
+  const int lane = threadIdx.x & 31;
+  const int n = A.n, k = A.k;
+  const int64_t rows = A.B * (int64_t)n;
+  const int64_t wstride = (int64_t)gridDim.x * (kUpdRowThreads / 32);
+  for (int64_t q = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5); q < rows; q += wstride) {
+    const int64_t b = q / n;
+    const int j = (int)(q - b * n);
+    const int act = A.act[b];
+    if (act == UPD_KEEP) continue;
+    T* Gj = A.g + q * n;
+    if (act == UPD_ZERO) {
+      for (int c = lane; c < n; c += 32) Gj[c] = s_zero<T>();
+      continue;
+    }
+    const T* U = A.u + b * (int64_t)k * n;
+    const T* H = A.h + b * (int64_t)k * n;
+    const int* id = A.idx + b * k;
+    T cf[kUpdMaxK];
+#pragma unroll
+    for (int r = 0; r < kUpdMaxK; ++r) {
+      cf[r] = s_zero<T>();
+      if (r < k) {
+        T v = warp_dot(U + (int64_t)r * n, Gj, n, lane);
+        if (__ldg(id + r) == j) v = sub(v, s_one<T>());
+        cf[r] = v;
+      }
+    }
+    for (int c = lane; c < n; c += 32) {
+      T x = Gj[c];
+#pragma unroll
+      for (int r = 0; r < kUpdMaxK; ++r)
+        if (r < k) x = fms(x, cf[r], H[(int64_t)r * n + c]);
+      Gj[c] = x;
+    }
+  }
+}
+
+}  // namespace fx

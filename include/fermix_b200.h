@@ -104,6 +104,28 @@ int fermix_slogdet_gather(void* stream, int dtype, int prec, int64_t batch, int6
                           size_t workspace_bytes);
 size_t fermix_slogdet_gather_workspace_bytes(int dtype, int prec, int64_t batch, int64_t n, int grad);
 
+/* Rank-k row replacement from the exported inverse (no reference counterpart; the
+ * single- and multi-electron moves of a QMC caller, built on the inverse that
+ * fermix_slogdet_grad exports -- _lu_parts, src/fermix/_inverse.py:502-531). g holds
+ * G = A^-T per matrix (fermix_slogdet_grad with coef NULL, conj_out 0, adjugate 0). A move
+ * replaces rows idx[b * k + r] (int32, distinct, in [0, n)) of A by rows[b, r, :]
+ * ((batch, k, n), same dtype), 0 <= k <= 16, k <= n.
+ *   fermix_slogdet_ratio:  (sign, logabs) of det(A') / det(A) = det(U A^-1 E), in the
+ *                          slogdet conventions (sign in the input dtype; a singular ratio
+ *                          gives (0, -inf); an index outside [0, n) gives NaN). Reads k
+ *                          rows of each G; no workspace.
+ *   fermix_slogdet_update: the same ratio, and G replaced in place by A'^-T (Woodbury) for
+ *                          every matrix with accept[b] != 0 (accept NULL = all). A member
+ *                          whose ratio is exactly 0 gets G' = 0, one with a bad index keeps
+ *                          G. rows must not overlap g. Workspace:
+ *                          fermix_slogdet_update_workspace_bytes. */
+int fermix_slogdet_ratio(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, const void* g,
+                         const void* rows, const int* idx, void* sign, void* logabs);
+int fermix_slogdet_update(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, void* g, const void* rows,
+                          const int* idx, const unsigned char* accept, void* sign, void* logabs, void* workspace,
+                          size_t workspace_bytes);
+size_t fermix_slogdet_update_workspace_bytes(int dtype, int64_t batch, int64_t n, int64_t k);
+
 /* Size of the fixed device array fermix_slogdet_grad_static uses instead of a workspace
  * (16 MiB, one copy per device, part of the library's device image). */
 #define FX_STATIC_SCRATCH_BYTES (16u << 20)

@@ -204,3 +204,30 @@ def test_oracle_matches_golden_fixtures():
     z = np.load(GOLDEN)
     for name in CASES:
         check_case(name, z, F)
+
+
+# ---------------------------------------------------------------- rank-k row moves
+@pytest.mark.parametrize("dtype", [np.float64, np.complex128])
+@pytest.mark.parametrize("n,k", [(1, 1), (6, 2), (20, 5), (40, 16)])
+def test_move_oracle_woodbury_matches_refactorisation(dtype, n, k):
+    """The Woodbury route of the move oracle (the kernels' algorithm) against refactoring
+    the moved matrix with the getrf restatement."""
+    from oracle import moves
+
+    rng = np.random.default_rng(n * 31 + k)
+    B = 3
+    A = rng.standard_normal((B, n, n))
+    U = rng.standard_normal((B, k, n))
+    if np.dtype(dtype).kind == "c":
+        A = A + 1j * rng.standard_normal((B, n, n))
+        U = U + 1j * rng.standard_normal((B, k, n))
+    A, U = A.astype(dtype), U.astype(dtype)
+    idx = np.stack([rng.choice(n, k, replace=False) for _ in range(B)])
+    G = np.swapaxes(np.linalg.inv(A), -1, -2)
+    s1, l1 = moves.ratio_direct(A, U, idx)
+    s2, l2 = moves.ratio_woodbury(G, U, idx)
+    assert np.allclose(l1, l2, rtol=0, atol=1e-10)
+    assert np.allclose(s1, s2, rtol=0, atol=1e-10)
+    G1 = moves.inverse_direct(A, U, idx)
+    G2 = moves.update_woodbury(G, U, idx)
+    assert np.abs(G1 - G2).max() <= 1e-9 * np.abs(G1).max()
