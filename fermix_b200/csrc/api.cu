@@ -669,10 +669,40 @@ int run_update(cudaStream_t s, int64_t batch, int64_t n, int64_t k, void* g, con
   upd_prep_kernel<T><<<(unsigned)(batch < pcap ? batch : pcap), kUpdPrepThreads, 0, s>>>(A);
   if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
   if (apply && k > 0) {
-    const int64_t wpb = kUpdRowThreads / 32;
-    const int64_t need = (batch * n + wpb - 1) / wpb, rcap = (int64_t)D->sms * 8;
-    upd_rows_kernel<T><<<(unsigned)(need < rcap ? need : rcap), kUpdRowThreads, 0, s>>>(A);
-    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+    const int64_t wpb = kUpdRowThreads / 32, rcap = (int64_t)D->sms * 8;
+    const size_t rowb = (size_t)n * sizeof(T);
+    const bool vec = rowb % 16 == 0 && rowb <= 8 * 512 &&
+                     ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u)) & 15) == 0;
+    if (vec) {
+      // pieces per lane, and rows per warp: 4 KB of G in flight per warp where k <= 4
+      const int ch = rowb <= 512 ? 1 : rowb <= 1024 ? 2 : rowb <= 2048 ? 4 : 8;
+      const int rw = k > 4 ? 1 : ch == 1 ? 4 : ch == 2 ? 2 : ch == 4 ? 2 : 1;
+      const int64_t need = (batch * ((n + rw - 1) / rw) + wpb - 1) / wpb;
+      const unsigned grid = (unsigned)(need < rcap ? need : rcap);
+      void* kern = nullptr;
+      if (k == 1) {
+        kern = ch == 1 ? (void*)&upd_rows_vec_kernel<T, 1, 4, 1>
+             : ch == 2 ? (void*)&upd_rows_vec_kernel<T, 2, 2, 1>
+             : ch == 4 ? (void*)&upd_rows_vec_kernel<T, 4, 2, 1>
+                       : (void*)&upd_rows_vec_kernel<T, 8, 1, 1>;
+      } else if (k <= 4) {
+        kern = ch == 1 ? (void*)&upd_rows_vec_kernel<T, 1, 4, 4>
+             : ch == 2 ? (void*)&upd_rows_vec_kernel<T, 2, 2, 4>
+             : ch == 4 ? (void*)&upd_rows_vec_kernel<T, 4, 2, 4>
+                       : (void*)&upd_rows_vec_kernel<T, 8, 1, 4>;
+      } else {
+        kern = ch == 1 ? (void*)&upd_rows_vec_kernel<T, 1, 1, kUpdMaxK>
+             : ch == 2 ? (void*)&upd_rows_vec_kernel<T, 2, 1, kUpdMaxK>
+             : ch == 4 ? (void*)&upd_rows_vec_kernel<T, 4, 1, kUpdMaxK>
+                       : (void*)&upd_rows_vec_kernel<T, 8, 1, kUpdMaxK>;
+      }
+      void* args[] = {&A};
+      if (cudaLaunchKernel(kern, dim3(grid), dim3(kUpdRowThreads), args, 0, s) != cudaSuccess) return FX_ERR_CUDA;
+    } else {
+      const int64_t need = (batch * n + wpb - 1) / wpb;
+      upd_rows_kernel<T><<<(unsigned)(need < rcap ? need : rcap), kUpdRowThreads, 0, s>>>(A);
+      if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+    }
   }
   return FX_OK;
 }

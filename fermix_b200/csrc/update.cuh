@@ -14,10 +14,13 @@
 //   fixed-order lane partials and an xor tree), its LU with partial pivoting by one thread
 //   (k <= 16, first-occurrence argmax of abs1 as the reference's LU) giving the ratio's
 //   (sign, logabs), then R^-1 and H into the workspace, and the matrix's row-kernel action.
-// upd_rows_kernel: one warp per row of G, in place: the k dot products V[.][j], then the row
-//   update. The row is read twice by the same warp (the second read hits L1 / L2); H and U
-//   are shared by all rows of a matrix and stay cache-resident, so HBM sees one read and
-//   one write of G: the kernel is HBM-bound at n^2 (read) + n^2 (write) elements.
+// upd_rows_vec_kernel: rows of up to 4 KB whose bytes are a multiple of 16 (16-byte aligned
+//   arrays): one warp holds RW rows of one matrix in registers as 16-byte pieces (lane l owns
+//   pieces l, l + 32, ...), forms their k dot products V[.][j] from the same registers, updates
+//   them and stores them. Each G element is read once and written once; U and H, shared by
+//   the matrix's rows, stay L1 / L2 resident. HBM-bound at n^2 (read) + n^2 (write) elements.
+// upd_rows_kernel: any other shape: one warp per row, scalar column loop, the row read twice
+//   (the second read hits L1 / L2).
 #pragma once
 #include "scalar.cuh"
 
@@ -88,7 +91,7 @@ __device__ __forceinline__ c128_t warp_sum_t<c128_t>(c128_t v) {
 }
 
 // x . y over n entries: lane partials in column order, then the xor tree (every lane
-// returns the same bits; the rows kernel uses the same order, so V[r][idx_s] == R[r][s]).
+// returns the same bits).
 template <typename T>
 __device__ __forceinline__ T warp_dot(const T* __restrict__ x, const T* __restrict__ y, int n, int lane) {
   T acc = s_zero<T>();
@@ -257,6 +260,106 @@ __global__ void __launch_bounds__(kUpdRowThreads) upd_rows_kernel(UpdArgs<T> A) 
         if (r < k) x = fms(x, cf[r], H[(int64_t)r * n + c]);
       Gj[c] = x;
     }
+  }
+}
+
+// 16 bytes of consecutive elements: the unit of the vector row kernel
+template <typename T>
+struct alignas(16) UpdPiece {
+  T v[16 / sizeof(T)];
+};
+
+// CH: 16-byte pieces per lane (row bytes <= CH * 512); RW: rows per warp; KM: the largest k
+template <typename T, int CH, int RW, int KM>
+__global__ void __launch_bounds__(kUpdRowThreads, KM <= 4 ? 2 : 1) upd_rows_vec_kernel(UpdArgs<T> A) {
+  constexpr int E = 16 / (int)sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int n = A.n, k = A.k;
+  const int np = n / E;  // pieces per row
+  const int gpm = (n + RW - 1) / RW;
+  const int64_t groups = A.B * gpm;
+  const int64_t wstride = (int64_t)gridDim.x * (kUpdRowThreads / 32);
+  for (int64_t q = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5); q < groups; q += wstride) {
+    const int64_t b = q / gpm;
+    const int j0 = (int)(q - b * gpm) * RW;
+    const int act = A.act[b];
+    if (act == UPD_KEEP) continue;
+    UpdPiece<T>* Gp = reinterpret_cast<UpdPiece<T>*>(A.g + (b * n + j0) * (int64_t)n);
+    UpdPiece<T> x[RW][CH];
+#pragma unroll
+    for (int w = 0; w < RW; ++w)
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int p = c * 32 + lane;
+        if (p < np && j0 + w < n) {
+          x[w][c] = Gp[(int64_t)w * np + p];
+        } else {
+#pragma unroll
+          for (int e = 0; e < E; ++e) x[w][c].v[e] = s_zero<T>();
+        }
+      }
+    if (act == UPD_APPLY) {
+      const UpdPiece<T>* Up = reinterpret_cast<const UpdPiece<T>*>(A.u + b * (int64_t)k * n);
+      const UpdPiece<T>* Hp = reinterpret_cast<const UpdPiece<T>*>(A.h + b * (int64_t)k * n);
+      const int* id = A.idx + b * k;
+      T cf[RW][KM];
+#pragma unroll
+      for (int r = 0; r < KM; ++r) {
+        if (r < k) {
+          T acc[RW];
+#pragma unroll
+          for (int w = 0; w < RW; ++w) acc[w] = s_zero<T>();
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
+            const int p = c * 32 + lane;
+            if (p < np) {
+              const UpdPiece<T> u = Up[(int64_t)r * np + p];
+#pragma unroll
+              for (int e = 0; e < E; ++e)
+#pragma unroll
+                for (int w = 0; w < RW; ++w) acc[w] = fma_(u.v[e], x[w][c].v[e], acc[w]);
+            }
+          }
+          const int ir = __ldg(id + r);
+#pragma unroll
+          for (int w = 0; w < RW; ++w) {
+            T v = warp_sum_t<T>(acc[w]);
+            if (ir == j0 + w) v = sub(v, s_one<T>());
+            cf[w][r] = v;
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int p = c * 32 + lane;
+        if (p < np) {
+#pragma unroll
+          for (int r = 0; r < KM; ++r) {
+            if (r < k) {
+              const UpdPiece<T> h = Hp[(int64_t)r * np + p];
+#pragma unroll
+              for (int w = 0; w < RW; ++w)
+#pragma unroll
+                for (int e = 0; e < E; ++e) x[w][c].v[e] = fms(x[w][c].v[e], cf[w][r], h.v[e]);
+            }
+          }
+        }
+      }
+    } else {  // UPD_ZERO
+#pragma unroll
+      for (int w = 0; w < RW; ++w)
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+#pragma unroll
+          for (int e = 0; e < E; ++e) x[w][c].v[e] = s_zero<T>();
+    }
+#pragma unroll
+    for (int w = 0; w < RW; ++w)
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int p = c * 32 + lane;
+        if (p < np && j0 + w < n) Gp[(int64_t)w * np + p] = x[w][c];
+      }
   }
 }
 
