@@ -10,10 +10,11 @@
 //   G' = A'^-T = G - (V^T - E) H,  H = R^-T G[idx, :]   (Woodbury)
 // so row j of G' is G_j - sum_r (V[r][j] - [j == idx_r]) H_r.
 //
-// upd_prep_kernel: one 128-thread block per matrix. R by k^2 dot products (one warp each,
-//   fixed-order lane partials and an xor tree), its LU with partial pivoting by one thread
-//   (k <= 16, first-occurrence argmax of abs1 as the reference's LU) giving the ratio's
-//   (sign, logabs), then R^-1 and H into the workspace, and the matrix's row-kernel action.
+// upd_prep_kernel: one 128-thread block per matrix. R by k^2 dot products (fixed-order lane
+//   partials and an xor tree, four per warp at a time), then one warp runs Gauss-Jordan with
+//   partial pivoting on [R | I] (k <= 16, first-occurrence argmax of abs1 as the reference's
+//   LU; lane j holds column j), giving the ratio's (sign, logabs) and R^-1; then H into the
+//   workspace, and the matrix's row-kernel action.
 // upd_rows_vec_kernel: rows of up to 4 KB whose bytes are a multiple of 16 (16-byte aligned
 //   arrays): one warp holds RW rows of one matrix in registers as 16-byte pieces (lane l owns
 //   pieces l, l + 32, ...), forms their k dot products V[.][j] from the same registers, updates
@@ -101,19 +102,28 @@ __device__ __forceinline__ T warp_dot(const T* __restrict__ x, const T* __restri
 
 template <typename T>
 struct UpdSmem {
-  T r[kUpdMaxK][kUpdMaxK + 1];   // R, then its LU factors
+  T r[kUpdMaxK][kUpdMaxK + 1];   // R
   T ri[kUpdMaxK][kUpdMaxK + 1];  // R^-1
-  int piv[kUpdMaxK];
   int id[kUpdMaxK];
   int bad, sing;
 };
+
+// a[i] with i only known at run time, over a register array indexed by constants
+template <typename T>
+__device__ __forceinline__ T upd_pick(const T (&a)[kUpdMaxK], int i) {
+  T v = a[0];
+#pragma unroll
+  for (int q = 1; q < kUpdMaxK; ++q)
+    if (q == i) v = a[q];
+  return v;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kUpdPrepThreads) upd_prep_kernel(UpdArgs<T> A) {
   using R = typename Sc<T>::R;
   __shared__ UpdSmem<T> S;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n = A.n, k = A.k;
+  const int n = A.n, k = A.k, kk = A.k * A.k;
   for (int64_t b = blockIdx.x; b < A.B; b += gridDim.x) {
     const T* G = A.g + b * (int64_t)n * n;
     const T* U = A.u + b * (int64_t)k * n;
@@ -127,83 +137,115 @@ __global__ void __launch_bounds__(kUpdPrepThreads) upd_prep_kernel(UpdArgs<T> A)
     __syncthreads();
     const bool bad = S.bad != 0;
     if (!bad) {
-      for (int p = warp; p < k * k; p += kUpdPrepThreads / 32) {
-        const int r = p / k, s = p - r * k;
-        const T v = warp_dot(U + (int64_t)r * n, G + (int64_t)S.id[s] * n, n, lane);
-        if (lane == 0) S.r[r][s] = v;
+      // R[r][s] = U_r . G_{idx_s}: four dot products per warp at a time (lane partials in
+      // column order, then the xor tree)
+      for (int p0 = warp * 4; p0 < kk; p0 += kUpdPrepThreads / 32 * 4) {
+        T acc[4];
+        const T* ur[4];
+        const T* gr[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int p = p0 + q < kk ? p0 + q : 0;
+          const int r = p / k, sc = p - r * k;
+          ur[q] = U + (int64_t)r * n;
+          gr[q] = G + (int64_t)S.id[sc] * n;
+          acc[q] = s_zero<T>();
+        }
+        for (int c = lane; c < n; c += 32)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[q] = fma_(ur[q][c], gr[q][c], acc[q]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const T v = warp_sum_t<T>(acc[q]);
+          const int p = p0 + q;
+          if (lane == 0 && p < kk) S.r[p / k][p - (p / k) * k] = v;
+        }
       }
     }
     __syncthreads();
-    if (tid == 0) {
-      // LU with partial pivoting of R: sign = prod unit(pivot) * (-1)^swaps,
-      // logabs = sum log|pivot| in column order; a zero pivot gives (0, -inf)
+    if (warp == 0) {
+      // Gauss-Jordan with partial pivoting on [R | I], lane j holding column j: pivot = the
+      // first largest abs1 of column c in rows c .. k - 1 (lane c's registers); rows below c
+      // get the LU update a_i -= (a_ic / d) a_c, so the pivots, sign and logabs are those of
+      // the LU of R; the rows above get the same update, leaving [D | D R^-1] (row-permuted).
+      // sign = prod unit(pivot) * (-1)^swaps, logabs = sum log|pivot| in column order.
+      T a[kUpdMaxK], dd[kUpdMaxK];
+#pragma unroll
+      for (int i = 0; i < kUpdMaxK; ++i) {
+        T v = s_zero<T>();
+        if (!bad && i < k) {
+          if (lane < k) v = S.r[i][lane];
+          else if (lane - k == i) v = s_one<T>();
+        }
+        a[i] = v;
+        dd[i] = s_one<T>();
+      }
       T sg = s_one<T>();
       KSum<R> ls;
       ls.init();
       int sing = 0;
-      if (bad) {
-        sg = upd_nan<T>();
-      } else {
-        for (int c = 0; c < k; ++c) {
-          int p = c;
-          R best = abs1(S.r[c][c]);
-          for (int i = c + 1; i < k; ++i) {
-            const R m = abs1(S.r[i][c]);
-            if (m > best) {
-              best = m;
-              p = i;
+#pragma unroll
+      for (int c = 0; c < kUpdMaxK; ++c) {
+        if (bad || c >= k) continue;
+        int p = c;
+        if (lane == c) {
+          R best = abs1(a[c]);
+#pragma unroll
+          for (int i = c + 1; i < kUpdMaxK; ++i) {
+            if (i < k) {
+              const R m = abs1(a[i]);
+              if (m > best) {
+                best = m;
+                p = i;
+              }
             }
           }
-          S.piv[c] = p;
-          if (p != c) {
-            for (int j = 0; j < k; ++j) upd_swap(S.r[c][j], S.r[p][j]);
-            sg = neg(sg);
-          }
-          const T d = S.r[c][c];
-          if (is_zero(d)) {
-            sing = 1;
-            continue;
-          }
-          sg = mul(sg, unit(d));
-          ls.add(rlog(mag(d)));
-          const T dinv = recip(d);
-          for (int i = c + 1; i < k; ++i) {
-            const T l = mul(S.r[i][c], dinv);
-            S.r[i][c] = l;
-            for (int j = c + 1; j < k; ++j) S.r[i][j] = fms(S.r[i][j], l, S.r[c][j]);
+        }
+        p = __shfl_sync(0xffffffffu, p, c);
+        if (p != c) {
+          const T t = upd_pick(a, p);
+#pragma unroll
+          for (int i = c + 1; i < kUpdMaxK; ++i)
+            if (i == p) a[i] = a[c];
+          a[c] = t;
+          sg = neg(sg);
+        }
+        const T d = shfl_idx<T>(a[c], c);
+        dd[c] = d;
+        if (is_zero(d)) {
+          sing = 1;
+          continue;
+        }
+        sg = mul(sg, unit(d));
+        ls.add(rlog(mag(d)));
+        const T dinv = recip(d);
+#pragma unroll
+        for (int i = 0; i < kUpdMaxK; ++i) {
+          if (i != c && i < k) {
+            const T l = shfl_idx<T>(mul(a[i], dinv), c);  // lane c holds a_ic
+            a[i] = fms(a[i], l, a[c]);
           }
         }
       }
       R la = ls.value();
-      if (bad) la = R(NAN);
-      if (sing && !bad) {
+      if (bad) {
+        sg = upd_nan<T>();
+        la = R(NAN);
+      } else if (sing) {
         sg = s_zero<T>();
         la = -R(INFINITY);
       }
-      A.sign[b] = sg;
-      A.logabs[b] = la;
-      S.sing = sing;
-      if (A.h) {
-        const bool acc = A.accept == nullptr || A.accept[b] != 0;
-        A.act[b] = (!acc || bad) ? UPD_KEEP : (sing ? UPD_ZERO : UPD_APPLY);
-        if (acc && !bad && !sing) {
-          // R^-1 column by column: P R = L U, solve L y = P e_c, then U x = y
-          for (int c = 0; c < k; ++c) {
-            T y[kUpdMaxK];
-            for (int i = 0; i < k; ++i) y[i] = (i == c) ? s_one<T>() : s_zero<T>();
-            for (int i = 0; i < k; ++i) {
-              const int p = S.piv[i];
-              if (p != i) upd_swap(y[i], y[p]);
-            }
-            for (int i = 0; i < k; ++i)
-              for (int j = 0; j < i; ++j) y[i] = fms(y[i], S.r[i][j], y[j]);
-            for (int i = k - 1; i >= 0; --i) {
-              for (int j = i + 1; j < k; ++j) y[i] = fms(y[i], S.r[i][j], y[j]);
-              y[i] = sdiv(y[i], S.r[i][i]);
-            }
-            for (int i = 0; i < k; ++i) S.ri[i][c] = y[i];
-          }
-        }
+      const bool acc = A.accept == nullptr || A.accept[b] != 0;
+      if (lane == 0) {
+        A.sign[b] = sg;
+        A.logabs[b] = la;
+        S.sing = sing;
+        if (A.h) A.act[b] = (!acc || bad) ? UPD_KEEP : (sing ? UPD_ZERO : UPD_APPLY);
+      }
+      if (A.h && acc && !bad && !sing && lane >= k && lane < 2 * k) {
+#pragma unroll
+        for (int i = 0; i < kUpdMaxK; ++i)
+          if (i < k) S.ri[i][lane - k] = mul(a[i], recip(dd[i]));  // row i of R^-1 = row i / d_i
       }
     }
     __syncthreads();
@@ -212,10 +254,14 @@ __global__ void __launch_bounds__(kUpdPrepThreads) upd_prep_kernel(UpdArgs<T> A)
       T* H = A.h + b * (int64_t)k * n;
       for (int c = tid; c < n; c += kUpdPrepThreads) {
         T gs[kUpdMaxK];
-        for (int s = 0; s < k; ++s) gs[s] = G[(int64_t)S.id[s] * n + c];
+#pragma unroll
+        for (int s2 = 0; s2 < kUpdMaxK; ++s2)
+          if (s2 < k) gs[s2] = G[(int64_t)S.id[s2] * n + c];
         for (int r = 0; r < k; ++r) {
           T acc = s_zero<T>();
-          for (int s = 0; s < k; ++s) acc = fma_(S.ri[s][r], gs[s], acc);
+#pragma unroll
+          for (int s2 = 0; s2 < kUpdMaxK; ++s2)
+            if (s2 < k) acc = fma_(S.ri[s2][r], gs[s2], acc);
           H[(int64_t)r * n + c] = acc;
         }
       }
@@ -279,10 +325,15 @@ __global__ void __launch_bounds__(kUpdRowThreads, KM <= 4 ? 2 : 1) upd_rows_vec_
   const int gpm = (n + RW - 1) / RW;
   const int64_t groups = A.B * gpm;
   const int64_t wstride = (int64_t)gridDim.x * (kUpdRowThreads / 32);
-  for (int64_t q = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5); q < groups; q += wstride) {
+  // U and H do not depend on G: where registers allow they are loaded together with the rows
+  constexpr bool HOIST = KM * CH <= 4 && (KM == 1 || sizeof(T) <= 8);
+  int64_t q = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5);
+  int act_next = q < groups ? A.act[q / gpm] : UPD_KEEP;
+  for (; q < groups; q += wstride) {
     const int64_t b = q / gpm;
     const int j0 = (int)(q - b * gpm) * RW;
-    const int act = A.act[b];
+    const int act = act_next;
+    if (q + wstride < groups) act_next = A.act[(q + wstride) / gpm];  // in flight meanwhile
     if (act == UPD_KEEP) continue;
     UpdPiece<T>* Gp = reinterpret_cast<UpdPiece<T>*>(A.g + (b * n + j0) * (int64_t)n);
     UpdPiece<T> x[RW][CH];
@@ -302,6 +353,19 @@ __global__ void __launch_bounds__(kUpdRowThreads, KM <= 4 ? 2 : 1) upd_rows_vec_
       const UpdPiece<T>* Up = reinterpret_cast<const UpdPiece<T>*>(A.u + b * (int64_t)k * n);
       const UpdPiece<T>* Hp = reinterpret_cast<const UpdPiece<T>*>(A.h + b * (int64_t)k * n);
       const int* id = A.idx + b * k;
+      UpdPiece<T> uu[HOIST ? KM : 1][HOIST ? CH : 1], hh[HOIST ? KM : 1][HOIST ? CH : 1];
+      if constexpr (HOIST) {
+#pragma unroll
+        for (int r = 0; r < KM; ++r)
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
+            const int p = c * 32 + lane;
+            if (r < k && p < np) {
+              uu[r][c] = Up[(int64_t)r * np + p];
+              hh[r][c] = Hp[(int64_t)r * np + p];
+            }
+          }
+      }
       T cf[RW][KM];
 #pragma unroll
       for (int r = 0; r < KM; ++r) {
@@ -313,7 +377,7 @@ __global__ void __launch_bounds__(kUpdRowThreads, KM <= 4 ? 2 : 1) upd_rows_vec_
           for (int c = 0; c < CH; ++c) {
             const int p = c * 32 + lane;
             if (p < np) {
-              const UpdPiece<T> u = Up[(int64_t)r * np + p];
+              const UpdPiece<T> u = HOIST ? uu[HOIST ? r : 0][HOIST ? c : 0] : Up[(int64_t)r * np + p];
 #pragma unroll
               for (int e = 0; e < E; ++e)
 #pragma unroll
@@ -336,7 +400,7 @@ __global__ void __launch_bounds__(kUpdRowThreads, KM <= 4 ? 2 : 1) upd_rows_vec_
 #pragma unroll
           for (int r = 0; r < KM; ++r) {
             if (r < k) {
-              const UpdPiece<T> h = Hp[(int64_t)r * np + p];
+              const UpdPiece<T> h = HOIST ? hh[HOIST ? r : 0][HOIST ? c : 0] : Hp[(int64_t)r * np + p];
 #pragma unroll
               for (int w = 0; w < RW; ++w)
 #pragma unroll
