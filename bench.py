@@ -449,7 +449,9 @@ def run_move(a, rank, world, local):
                        "l2": "G exceeds L2 (no flush needed)" if B * n * n * s > 126e6 else "G fits L2"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "upd_rows_kernel", "algorithmic_bytes_per_launch": B * by},
+                         "kernel": "upd_rows_vec_kernel",
+                         "timing": "the whole call (ratio kernel + row kernel): an upper bound on the row kernel's time",
+                         "algorithmic_bytes_per_launch": B * by},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": a.steps * 2,

@@ -666,7 +666,12 @@ int run_update(cudaStream_t s, int64_t batch, int64_t n, int64_t k, void* g, con
     A.h = reinterpret_cast<T*>(static_cast<unsigned char*>(ws) + align256((size_t)batch * sizeof(int)));
   }
   const int64_t pcap = (int64_t)D->sms * 8;
-  upd_prep_kernel<T><<<(unsigned)(batch < pcap ? batch : pcap), kUpdPrepThreads, 0, s>>>(A);
+  if (k == 1) {
+    const int64_t need = (batch + kUpdRowThreads / 32 - 1) / (kUpdRowThreads / 32);
+    upd_prep1_kernel<T><<<(unsigned)(need < pcap ? need : pcap), kUpdRowThreads, 0, s>>>(A);
+  } else {
+    upd_prep_kernel<T><<<(unsigned)(batch < pcap ? batch : pcap), kUpdPrepThreads, 0, s>>>(A);
+  }
   if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
   if (apply && k > 0) {
     const int64_t wpb = kUpdRowThreads / 32, rcap = (int64_t)D->sms * 8;

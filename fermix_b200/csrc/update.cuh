@@ -10,7 +10,8 @@
 //   G' = A'^-T = G - (V^T - E) H,  H = R^-T G[idx, :]   (Woodbury)
 // so row j of G' is G_j - sum_r (V[r][j] - [j == idx_r]) H_r.
 //
-// upd_prep_kernel: one 128-thread block per matrix. R by k^2 dot products (fixed-order lane
+// upd_prep1_kernel (k = 1): one warp per matrix: R = U . G_idx, the ratio, H = G_idx / R.
+// upd_prep_kernel (k > 1): one 128-thread block per matrix. R by k^2 dot products (fixed-order lane
 //   partials and an xor tree, four per warp at a time), then one warp runs Gauss-Jordan with
 //   partial pivoting on [R | I] (k <= 16, first-occurrence argmax of abs1 as the reference's
 //   LU; lane j holds column j), giving the ratio's (sign, logabs) and R^-1; then H into the
@@ -107,6 +108,35 @@ struct UpdSmem {
   int id[kUpdMaxK];
   int bad, sing;
 };
+
+// k = 1: one warp per matrix. R = U . G_idx (the lane-partial / xor-tree dot), the ratio's
+// (sign, logabs) = (unit(R), log|R|), and H = R^-1 G_idx.
+template <typename T>
+__global__ void __launch_bounds__(kUpdRowThreads) upd_prep1_kernel(UpdArgs<T> A) {
+  using R = typename Sc<T>::R;
+  const int lane = threadIdx.x & 31;
+  const int n = A.n;
+  const int64_t wstride = (int64_t)gridDim.x * (kUpdRowThreads / 32);
+  for (int64_t b = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5); b < A.B; b += wstride) {
+    const int i = A.idx[b];
+    const bool bad = i < 0 || i >= n;
+    const T* Gi = A.g + (b * n + (bad ? 0 : i)) * (int64_t)n;
+    T d = s_zero<T>();
+    if (!bad) d = warp_dot(A.u + b * (int64_t)n, Gi, n, lane);
+    const bool sing = !bad && is_zero(d);
+    const bool acc = A.accept == nullptr || A.accept[b] != 0;
+    if (lane == 0) {
+      A.sign[b] = bad ? upd_nan<T>() : (sing ? s_zero<T>() : unit(d));
+      A.logabs[b] = bad ? R(NAN) : (sing ? -R(INFINITY) : rlog(mag(d)));
+      if (A.h) A.act[b] = (!acc || bad) ? UPD_KEEP : (sing ? UPD_ZERO : UPD_APPLY);
+    }
+    if (A.h && acc && !bad && !sing) {
+      const T ri = recip(d);
+      T* H = A.h + b * (int64_t)n;
+      for (int c = lane; c < n; c += 32) H[c] = mul(ri, Gi[c]);
+    }
+  }
+}
 
 // a[i] with i only known at run time, over a register array indexed by constants
 template <typename T>
