@@ -16,6 +16,8 @@ from .api import (
     slogdet_gather,
     slogdet_ratio,
     slogdet_update,
+    slogpf_ratio,
+    slogpf_update,
     slogdet_parts,
     slogpf,
     slogpf_parts,
@@ -34,6 +36,8 @@ __all__ = [
     "slogdet_gather",
     "slogdet_ratio",
     "slogdet_update",
+    "slogpf_ratio",
+    "slogpf_update",
     "FermixFallbackWarning",
     "__version__",
 ]

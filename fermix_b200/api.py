@@ -463,6 +463,79 @@ def slogdet_update(g, rows, idx, *, accept=None, inplace=False):
     return sign.reshape(batch), logabs.reshape(batch), (g if inplace else G.reshape(g.shape))
 
 
+def _pf_move_args(g, row, idx):
+    """Checks of the Pfaffian move functions: g (..., n, n), row (..., n), idx (...)."""
+    g = _prep(g)
+    n = g.shape[-1]
+    if n < 2:
+        raise ValueError("a Pfaffian move needs n >= 2")
+    batch = tuple(g.shape[:-2])
+    row = torch.as_tensor(row, device=g.device)
+    if row.dtype != g.dtype:
+        raise TypeError(f"row must have the dtype of g ({g.dtype}), got {row.dtype}")
+    if tuple(row.shape) != batch + (n,):
+        raise ValueError(f"row must have shape {batch + (n,)}, got {tuple(row.shape)}")
+    if not isinstance(idx, torch.Tensor):
+        idx = torch.as_tensor(np.asarray(idx))
+    if idx.dtype not in (torch.int32, torch.int64, torch.int16, torch.uint8):
+        raise TypeError("idx must be an integer tensor")
+    if tuple(idx.shape) != batch:
+        raise ValueError(f"idx must have shape {batch}, got {tuple(idx.shape)}")
+    B = int(np.prod(batch)) if batch else 1
+    U = row.detach().reshape(B, n).contiguous()
+    I = idx.to(device=g.device, dtype=torch.int32).reshape(B).contiguous()
+    return g, U, I, batch, B, n
+
+
+def slogpf_ratio(g, row, idx):
+    """Pfaffian ratio of a one-index move (no reference counterpart: the one-electron move
+    of a Pfaffian wavefunction). ``g`` (..., n, n) holds S^-T / 2 -- the gradient
+    ``slogpf_parts`` returns -- and the move replaces row ``idx`` of the skew S by ``row``
+    (..., n) and column ``idx`` by -row (row[idx] is ignored). Returns (sign, logabs) of
+    pf(S') / pf(S) = 2 g[idx] . row in the slogpf conventions; reads one row of each g."""
+    g, U, I, batch, B, n = _pf_move_args(g, row, idx)
+    G = g.detach().reshape(B, n, n).contiguous()
+    sign = torch.empty(B, dtype=g.dtype, device=g.device)
+    logabs = torch.empty(B, dtype=_real(g.dtype), device=g.device)
+    with torch.cuda.device(g.device):
+        st = _lib.lib().fermix_slogpf_ratio(_stream_ptr(g.device), _KIND[g.dtype], B, n, _ptr(G), _ptr(U), _ptr(I),
+                                            _ptr(sign), _ptr(logabs))
+    _lib.check(st)
+    return sign.reshape(batch), logabs.reshape(batch)
+
+
+def slogpf_update(g, row, idx, *, accept=None, inplace=False):
+    """Apply a one-index Pfaffian move to the gradient: as ``slogpf_ratio``, and also
+    g <- S'^-T / 2 (rank-2 skew Woodbury) where ``accept`` (bool, shape g.shape[:-2]; None =
+    all) is true; the others keep g. A member whose ratio is exactly 0 gets a zero matrix.
+    Returns (sign, logabs, g_new); with ``inplace=True`` g (a contiguous CUDA tensor) is
+    updated and returned. Not differentiable."""
+    g, U, I, batch, B, n = _pf_move_args(g, row, idx)
+    if inplace:
+        if not g.is_contiguous():
+            raise ValueError("inplace=True needs a contiguous g")
+        G = g.detach().view(B, n, n)
+    else:
+        G = g.detach().reshape(B, n, n).clone()
+    acc = None
+    if accept is not None:
+        acc = torch.as_tensor(accept, device=g.device)
+        if tuple(acc.shape) != batch:
+            raise ValueError(f"accept must have shape {batch}, got {tuple(acc.shape)}")
+        acc = acc.to(torch.uint8).reshape(B).contiguous()
+    sign = torch.empty(B, dtype=g.dtype, device=g.device)
+    logabs = torch.empty(B, dtype=_real(g.dtype), device=g.device)
+    L = _lib.lib()
+    kind = _KIND[g.dtype]
+    with torch.cuda.device(g.device):
+        nbytes = L.fermix_slogpf_update_workspace_bytes(kind, B, n)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=g.device) if nbytes else None
+        st = L.fermix_slogpf_update(_stream_ptr(g.device), kind, B, n, _ptr(G), _ptr(U), _ptr(I), _ptr(acc),
+                                    _ptr(sign), _ptr(logabs), _ptr(ws), nbytes)
+    _lib.check(st)
+    return sign.reshape(batch), logabs.reshape(batch), (g if inplace else G.reshape(g.shape))
+
+
 def slogdet(a, *, prec=None, unroll_steps=None, block=None):
     """Sign and log|det| of a batch of matrices ``a`` of shape (..., n, n)
     (src/fermix/api.py:148-174). Returns (sign, logabsdet): sign has the dtype of ``a``

@@ -712,6 +712,54 @@ int run_update(cudaStream_t s, int64_t batch, int64_t n, int64_t k, void* g, con
   return FX_OK;
 }
 
+template <typename T>
+size_t pfm_ws_bytes(int64_t batch, int64_t n) {
+  return align256((size_t)batch * sizeof(int)) + align256((size_t)batch * sizeof(T)) +
+         2 * align256((size_t)batch * n * sizeof(T));
+}
+
+// Pfaffian one-index move: ratio only (apply == false) or ratio plus the in-place update
+template <typename T>
+int run_pf_move(cudaStream_t s, int64_t batch, int64_t n, void* g, const void* u, const int* idx,
+                const unsigned char* accept, void* sign, void* logabs, void* ws, size_t wsb, bool apply) {
+  const DevInfo* D = dev_info();
+  if (!D) return FX_ERR_DEVICE;
+  PfMoveArgs<T> A;
+  A.g = static_cast<T*>(g);
+  A.u = static_cast<const T*>(u);
+  A.idx = idx;
+  A.accept = accept;
+  A.sign = static_cast<T*>(sign);
+  A.logabs = static_cast<typename Sc<T>::R*>(logabs);
+  A.h = A.v = A.rho = nullptr;
+  A.act = nullptr;
+  A.B = batch;
+  A.n = (int)n;
+  if (apply) {
+    if (!ws || wsb < pfm_ws_bytes<T>(batch, n)) return FX_ERR_WORKSPACE;
+    unsigned char* p = static_cast<unsigned char*>(ws);
+    A.act = reinterpret_cast<int*>(p);
+    p += align256((size_t)batch * sizeof(int));
+    A.rho = reinterpret_cast<T*>(p);
+    p += align256((size_t)batch * sizeof(T));
+    A.h = reinterpret_cast<T*>(p);
+    p += align256((size_t)batch * n * sizeof(T));
+    A.v = reinterpret_cast<T*>(p);
+  }
+  const int64_t wpb = kUpdRowThreads / 32, cap = (int64_t)D->sms * 8;
+  const int64_t gp = (batch + wpb - 1) / wpb;
+  pfm_prep_kernel<T><<<(unsigned)(gp < cap ? gp : cap), kUpdRowThreads, 0, s>>>(A);
+  if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  if (apply) {
+    const int64_t gr = (batch * n + wpb - 1) / wpb;
+    pfm_v_kernel<T><<<(unsigned)(gr < cap ? gr : cap), kUpdRowThreads, 0, s>>>(A);
+    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+    pfm_rows_kernel<T><<<(unsigned)(gr < cap ? gr : cap), kUpdRowThreads, 0, s>>>(A);
+    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  }
+  return FX_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -839,6 +887,43 @@ const char* fermix_strerror(int code) {
 }
 
 int fermix_version(void) { return 100; }
+
+int fermix_slogpf_ratio(void* stream, int dtype, int64_t batch, int64_t n, const void* g, const void* row,
+                        const int* idx, void* sign, void* logabs) {
+  int e = validate(dtype, FX_PREC_DEFAULT, batch, n);
+  if (e) return e;
+  if (n < 2) return FX_ERR_SHAPE;
+  if (batch == 0) return FX_OK;
+  if (!g || !row || !idx || !sign || !logabs) return FX_ERR_NULL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_pf_move<T>(s, batch, n, const_cast<void*>(g), row, idx, nullptr, sign, logabs, nullptr, 0, false);
+  });
+}
+
+int fermix_slogpf_update(void* stream, int dtype, int64_t batch, int64_t n, void* g, const void* row, const int* idx,
+                         const unsigned char* accept, void* sign, void* logabs, void* workspace,
+                         size_t workspace_bytes) {
+  int e = validate(dtype, FX_PREC_DEFAULT, batch, n);
+  if (e) return e;
+  if (n < 2) return FX_ERR_SHAPE;
+  if (batch == 0) return FX_OK;
+  if (!g || !row || !idx || !sign || !logabs) return FX_ERR_NULL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_pf_move<T>(s, batch, n, g, row, idx, accept, sign, logabs, workspace, workspace_bytes, true);
+  });
+}
+
+size_t fermix_slogpf_update_workspace_bytes(int dtype, int64_t batch, int64_t n) {
+  if (validate(dtype, FX_PREC_DEFAULT, batch, n) || batch == 0 || n < 2) return 0;
+  return (size_t)by_dtype(dtype, [&](auto t) -> int {
+    using T = decltype(t);
+    return (int)((pfm_ws_bytes<T>(batch, n) + 255) / 256);
+  }) * 256;
+}
 
 int fermix_slogdet_ratio(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, const void* g,
                          const void* rows, const int* idx, void* sign, void* logabs) {

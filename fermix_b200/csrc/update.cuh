@@ -339,6 +339,119 @@ __global__ void __launch_bounds__(kUpdRowThreads) upd_rows_kernel(UpdArgs<T> A) 
   }
 }
 
+// ---------------------------------------------------------------- Pfaffian moves (k = 1)
+// A one-electron move of a Pfaffian wavefunction replaces row and column i of the skew S by
+// u and -u (u_i is ignored: the skew diagonal stays 0). The state is the slogpf gradient
+// G = S^-T / 2 = -S^-1 / 2 (fermix_slogpf_grad, adjugate 0). With g_i = row i of G and
+// v = G u, the rank-2 skew Woodbury identity gives
+//   pf(S') / pf(S) = rho = 2 g_i . u,
+//   G' = G + (y g_i^T - g_i y^T) / rho,  y = e_i - 2 v,
+// i.e. row j of G' is G_j + ((d_ij - 2 v_j) g_i - g_ij y) / rho. Every row needs the whole
+// of v, so the update takes three launches: the ratio (and a snapshot of g_i), v, the rows.
+template <typename T>
+struct PfMoveArgs {
+  T* g;                         // (B, n, n) G = S^-T / 2, updated in place
+  const T* u;                   // (B, n) the new row of S
+  const int* idx;               // (B,) the moved index i
+  const unsigned char* accept;  // (B,) or null = all
+  T* sign;                      // (B,) sign of pf(S') / pf(S)
+  typename Sc<T>::R* logabs;    // (B,) log |pf(S') / pf(S)|
+  T* h;                         // (B, n) workspace: g_i
+  T* v;                         // (B, n) workspace: G u
+  T* rho;                       // (B,) workspace: the ratio
+  int* act;                     // (B,) workspace: UPD_KEEP / UPD_APPLY / UPD_ZERO
+  int64_t B;
+  int n;
+};
+
+// x . y over n entries with entry `skip` left out
+template <typename T>
+__device__ __forceinline__ T warp_dot_skip(const T* __restrict__ x, const T* __restrict__ y, int n, int skip,
+                                           int lane) {
+  T acc = s_zero<T>();
+  for (int c = lane; c < n; c += 32)
+    if (c != skip) acc = fma_(x[c], y[c], acc);
+  return warp_sum_t<T>(acc);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kUpdRowThreads) pfm_prep_kernel(PfMoveArgs<T> A) {
+  using R = typename Sc<T>::R;
+  const int lane = threadIdx.x & 31;
+  const int n = A.n;
+  const int64_t wstride = (int64_t)gridDim.x * (kUpdRowThreads / 32);
+  for (int64_t b = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5); b < A.B; b += wstride) {
+    const int i = A.idx[b];
+    const bool bad = i < 0 || i >= n;
+    const T* Gi = A.g + (b * n + (bad ? 0 : i)) * (int64_t)n;
+    T d = s_zero<T>();
+    if (!bad) {
+      d = warp_dot_skip(Gi, A.u + b * (int64_t)n, n, i, lane);
+      d = add(d, d);
+    }
+    const bool sing = !bad && is_zero(d);
+    const bool acc = A.accept == nullptr || A.accept[b] != 0;
+    if (lane == 0) {
+      A.sign[b] = bad ? upd_nan<T>() : (sing ? s_zero<T>() : unit(d));
+      A.logabs[b] = bad ? R(NAN) : (sing ? -R(INFINITY) : rlog(mag(d)));
+      if (A.h) {
+        A.act[b] = (!acc || bad) ? UPD_KEEP : (sing ? UPD_ZERO : UPD_APPLY);
+        A.rho[b] = d;
+      }
+    }
+    if (A.h && acc && !bad && !sing)
+      for (int c = lane; c < n; c += 32) A.h[b * (int64_t)n + c] = Gi[c];
+  }
+}
+
+// v_j = G_j . u (u_i left out), one warp per row of the matrices that apply the move
+template <typename T>
+__global__ void __launch_bounds__(kUpdRowThreads) pfm_v_kernel(PfMoveArgs<T> A) {
+  const int lane = threadIdx.x & 31;
+  const int n = A.n;
+  const int64_t rows = A.B * (int64_t)n;
+  const int64_t wstride = (int64_t)gridDim.x * (kUpdRowThreads / 32);
+  for (int64_t q = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5); q < rows; q += wstride) {
+    const int64_t b = q / n;
+    if (A.act[b] != UPD_APPLY) continue;
+    const T vj = warp_dot_skip(A.g + q * n, A.u + b * (int64_t)n, n, A.idx[b], lane);
+    if (lane == 0) A.v[q] = vj;
+  }
+}
+
+// G_j += ((d_ij - 2 v_j) g_i - g_ij (e_i - 2 v)) / rho, in place, one warp per row
+template <typename T>
+__global__ void __launch_bounds__(kUpdRowThreads) pfm_rows_kernel(PfMoveArgs<T> A) {
+  const int lane = threadIdx.x & 31;
+  const int n = A.n;
+  const int64_t rows = A.B * (int64_t)n;
+  const int64_t wstride = (int64_t)gridDim.x * (kUpdRowThreads / 32);
+  for (int64_t q = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5); q < rows; q += wstride) {
+    const int64_t b = q / n;
+    const int j = (int)(q - b * n);
+    const int act = A.act[b];
+    if (act == UPD_KEEP) continue;
+    T* Gj = A.g + q * n;
+    if (act == UPD_ZERO) {
+      for (int c = lane; c < n; c += 32) Gj[c] = s_zero<T>();
+      continue;
+    }
+    const int i = A.idx[b];
+    const T ri = recip(A.rho[b]);
+    const T* h = A.h + b * (int64_t)n;
+    const T* v = A.v + b * (int64_t)n;
+    T c1 = neg(add(v[j], v[j]));
+    if (j == i) c1 = add(c1, s_one<T>());
+    c1 = mul(c1, ri);                 // (d_ij - 2 v_j) / rho
+    const T c2 = neg(mul(h[j], ri));  // -g_ij / rho
+    for (int c = lane; c < n; c += 32) {
+      T y = neg(add(v[c], v[c]));
+      if (c == i) y = add(y, s_one<T>());
+      Gj[c] = fma_(c2, y, fma_(c1, h[c], Gj[c]));
+    }
+  }
+}
+
 // 16 bytes of consecutive elements: the unit of the vector row kernel
 template <typename T>
 struct alignas(16) UpdPiece {

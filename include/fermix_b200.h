@@ -126,6 +126,27 @@ int fermix_slogdet_update(void* stream, int dtype, int64_t batch, int64_t n, int
                           size_t workspace_bytes);
 size_t fermix_slogdet_update_workspace_bytes(int dtype, int64_t batch, int64_t n, int64_t k);
 
+/* One-index Pfaffian move (no reference counterpart; the one-electron move of a Pfaffian
+ * wavefunction, on the gradient fermix_slogpf_grad exports -- _pf_parts,
+ * src/fermix/_pfinv.py:196-269). g holds G = S^-T / 2 per matrix (fermix_slogpf_grad with
+ * coef NULL, conj_out 0, adjugate 0). The move replaces row idx[b] of the skew S by
+ * row[b, :] ((batch, n), same dtype) and column idx[b] by -row[b, :]; row[b, idx[b]] is
+ * ignored (the diagonal stays 0). n >= 2.
+ *   fermix_slogpf_ratio:  (sign, logabs) of pf(S') / pf(S) = 2 G_i . u in the slogpf
+ *                         conventions (0, -inf when it is 0; NaN for an index outside
+ *                         [0, n)). Reads one row of each G; no workspace.
+ *   fermix_slogpf_update: the same ratio, and G replaced in place by S'^-T / 2 (rank-2 skew
+ *                         Woodbury) for every matrix with accept[b] != 0 (accept NULL = all);
+ *                         a member whose ratio is exactly 0 gets G' = 0, one with a bad index
+ *                         keeps G. row must not overlap g. Workspace:
+ *                         fermix_slogpf_update_workspace_bytes. */
+int fermix_slogpf_ratio(void* stream, int dtype, int64_t batch, int64_t n, const void* g, const void* row,
+                        const int* idx, void* sign, void* logabs);
+int fermix_slogpf_update(void* stream, int dtype, int64_t batch, int64_t n, void* g, const void* row, const int* idx,
+                         const unsigned char* accept, void* sign, void* logabs, void* workspace,
+                         size_t workspace_bytes);
+size_t fermix_slogpf_update_workspace_bytes(int dtype, int64_t batch, int64_t n);
+
 /* Size of the fixed device array fermix_slogdet_grad_static uses instead of a workspace
  * (16 MiB, one copy per device, part of the library's device image). */
 #define FX_STATIC_SCRATCH_BYTES (16u << 20)

@@ -12,12 +12,19 @@ float64 / complex128:
   det(A') / det(A) = det(U A^-1 E) and G' = G - (V^T - E) R^-T G[idx, :] with V = U A^-1,
   which is the algorithm the CUDA kernels implement.
 
+The Pfaffian one-index moves (row and column i of a skew S replaced by u and -u) follow the
+same pattern: ``pf_ratio_direct`` / ``pf_grad_direct`` refactor S' with the Parlett-Reid
+restatement (``oracle.fallback.slogpf``, ``src/fermix/_fallback.py:266-300``) and take
+S'^-T / 2; ``pf_ratio_woodbury`` / ``pf_update_woodbury`` use G = S^-T / 2 alone:
+pf(S') / pf(S) = 2 G_i . u and G' = G + (y g_i^T - g_i y^T) / rho, y = e_i - 2 G u.
+
 The tests pin the second route against the first, then the CUDA path against both.
 """
 
 import numpy as np
 
 from .fallback import slogdet as _slogdet
+from .fallback import slogpf as _slogpf
 
 
 def _wide(x):
@@ -71,3 +78,53 @@ def update_woodbury(G, rows, idx):
     E = np.zeros(V.shape, dtype=V.dtype)
     np.put_along_axis(E, I[..., :, None], 1.0, axis=-1)
     return G - np.einsum("...rj,...rc->...jc", V - E, H)
+
+
+def pf_apply_move(S, row, idx):
+    """S' = S with row idx[b] replaced by row[b] and column idx[b] by -row[b] (diagonal 0)."""
+    S = np.array(S, copy=True)
+    B = S.reshape((-1,) + S.shape[-2:])
+    U = np.asarray(row).reshape(B.shape[0], -1)
+    I = np.asarray(idx).reshape(-1)
+    for b in range(B.shape[0]):
+        u = U[b].copy()
+        u[I[b]] = 0
+        B[b, I[b], :] = u
+        B[b, :, I[b]] = -u
+    return B.reshape(S.shape)
+
+
+def pf_ratio_direct(S, row, idx):
+    """(sign, logabs) of pf(S') / pf(S) by refactoring both (float64 / complex128)."""
+    S = _wide(S)
+    s0, l0 = _slogpf(S)
+    s1, l1 = _slogpf(pf_apply_move(S, _wide(row), idx))
+    return s1 / np.where(s0 == 0, 1, s0), l1 - l0
+
+
+def pf_grad_direct(S, row, idx):
+    """S'^-T / 2 (float64 / complex128)."""
+    return 0.5 * np.swapaxes(np.linalg.inv(pf_apply_move(_wide(S), _wide(row), idx)), -1, -2)
+
+
+def pf_ratio_woodbury(G, row, idx):
+    """rho = 2 G_i . u (u_i left out)."""
+    G, U = _wide(G), _wide(row).copy()
+    I = np.asarray(idx)
+    np.put_along_axis(U, I[..., None], 0, axis=-1)
+    gi = np.take_along_axis(G, I[..., None, None].repeat(G.shape[-1], -1), axis=-2)[..., 0, :]
+    return 2 * np.sum(gi * U, axis=-1)
+
+
+def pf_update_woodbury(G, row, idx):
+    """G' = G + (y g_i^T - g_i y^T) / rho, y = e_i - 2 G u."""
+    G, U = _wide(G), _wide(row).copy()
+    I = np.asarray(idx)
+    n = G.shape[-1]
+    np.put_along_axis(U, I[..., None], 0, axis=-1)
+    gi = np.take_along_axis(G, I[..., None, None].repeat(n, -1), axis=-2)[..., 0, :]
+    rho = 2 * np.sum(gi * U, axis=-1)
+    y = -2 * np.einsum("...jc,...c->...j", G, U)
+    np.put_along_axis(y, I[..., None], np.take_along_axis(y, I[..., None], -1) + 1, axis=-1)
+    upd = np.einsum("...j,...c->...jc", y, gi) - np.einsum("...j,...c->...jc", gi, y)
+    return G + upd / rho[..., None, None]

@@ -139,3 +139,72 @@ def test_argument_errors():
                          torch.zeros((2, 1), dtype=torch.int32))
     with pytest.raises(ValueError):
         fx.slogdet_ratio(G, torch.zeros((2, 1, 8), device="cuda"), torch.zeros((2, 2), dtype=torch.int32))
+
+
+# ---------------------------------------------------------------- Pfaffian one-index moves
+def _pf_case(dtype, B, n, seed):
+    """A skew S (well conditioned: a block-diagonal [[0, 2], [-2, 0]] shift), G = S^-T / 2 in
+    float64 cast to dtype, and a new row near the old row idx."""
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((B, n, n)) / np.sqrt(n)
+    if np.dtype(dtype).kind == "c":
+        X = X + 1j * rng.standard_normal((B, n, n)) / np.sqrt(n)
+    J = np.zeros((n, n))
+    for q in range(0, n - 1, 2):
+        J[q, q + 1], J[q + 1, q] = 2.0, -2.0
+    S = X - np.swapaxes(X, -1, -2) + J
+    idx = rng.integers(0, n, size=B).astype(np.int32)
+    U = S[np.arange(B), idx] + 0.3 * (rng.standard_normal((B, n)) / np.sqrt(n))
+    G = 0.5 * np.swapaxes(np.linalg.inv(S), -1, -2)
+    return S, G.astype(dtype), U.astype(dtype), idx
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=IDS)
+@pytest.mark.parametrize("n", [2, 8, 34, 128, 300])
+def test_pf_move_matches_refactorisation(dtype, n):
+    S, G, U, idx = _pf_case(dtype, 6, n, seed=n + 7)
+    s, l = fx.slogpf_ratio(cuda(G), cuda(U), cuda(idx))
+    s_ref, l_ref = moves.pf_ratio_direct(S, U, idx)
+    tol = 1e-4 if _is32(dtype) else 1e-10
+    assert np.abs(host(l) - l_ref).max() <= tol * max(1.0, np.abs(l_ref).max())
+    if np.dtype(dtype).kind == "c":
+        assert np.abs(host(s) - s_ref).max() <= (1e-4 if _is32(dtype) else 1e-10)
+    else:
+        assert np.array_equal(host(s), s_ref.astype(host(s).dtype))
+    s2, l2, G2 = fx.slogpf_update(cuda(G), cuda(U), cuda(idx))
+    assert np.array_equal(host(s2), host(s)) and np.array_equal(host(l2), host(l))
+    gt = 1e-3 if _is32(dtype) else 1e-8
+    assert _relerr(host(G2), moves.pf_grad_direct(S, U, idx)) < gt
+    assert _relerr(host(G2), moves.pf_update_woodbury(G, U, idx)) < gt
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.complex128], ids=["f32", "c128"])
+def test_pf_move_walk_accept_singular_bad_index(dtype):
+    n, B = 40, 4
+    rng = np.random.default_rng(21)
+    S, G, _, _ = _pf_case(dtype, B, n, seed=5)
+    g = cuda(G)
+    cur = S.astype(np.complex128 if np.dtype(dtype).kind == "c" else np.float64)
+    total = np.zeros(B)
+    for step in range(15):
+        idx = rng.integers(0, n, size=B).astype(np.int32)
+        U = (cur[np.arange(B), idx] + 0.3 * rng.standard_normal((B, n)) / np.sqrt(n)).astype(dtype)
+        acc = rng.random(B) < 0.7
+        _, l, _ = fx.slogpf_update(g, cuda(U), cuda(idx), accept=cuda(acc), inplace=True)
+        total += np.where(acc, host(l), 0.0)
+        nxt = moves.pf_apply_move(cur, U, idx)
+        cur = np.where(acc[:, None, None], nxt, cur)
+    s0, l0 = moves._slogpf(S.astype(cur.dtype))
+    s1, l1 = moves._slogpf(cur)
+    tol = 1e-3 if _is32(dtype) else 1e-9
+    assert np.abs(total - (l1 - l0)).max() <= tol * max(1.0, np.abs(l1 - l0).max())
+    ref = 0.5 * np.swapaxes(np.linalg.inv(cur), -1, -2)
+    assert _relerr(host(g), ref) < (2e-3 if _is32(dtype) else 1e-8)
+    # a zero row gives ratio 0 -> (0, -inf) and G' = 0; an out-of-range index -> NaN, G kept
+    U = np.zeros((B, n), dtype=dtype)
+    idx = np.array([0, n, 1, 2], dtype=np.int32)
+    U[2:] = (cur[np.arange(2, 4), idx[2:]]).astype(dtype)
+    s, l, out = fx.slogpf_update(cuda(G), cuda(U), cuda(idx))
+    s, l, out = host(s), host(l), host(out)
+    assert s[0] == 0 and l[0] == -np.inf and np.all(out[0] == 0)
+    assert np.isnan(l[1]) and np.array_equal(out[1], G[1])

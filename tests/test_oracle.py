@@ -231,3 +231,29 @@ def test_move_oracle_woodbury_matches_refactorisation(dtype, n, k):
     G1 = moves.inverse_direct(A, U, idx)
     G2 = moves.update_woodbury(G, U, idx)
     assert np.abs(G1 - G2).max() <= 1e-9 * np.abs(G1).max()
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.complex128])
+@pytest.mark.parametrize("n", [2, 6, 20])
+def test_pf_move_oracle_woodbury_matches_refactorisation(dtype, n):
+    """The Pfaffian one-index move: the rank-2 skew Woodbury route against refactoring S'
+    with the Parlett-Reid restatement."""
+    from oracle import moves
+
+    rng = np.random.default_rng(n)
+    B = 3
+    A = rng.standard_normal((B, n, n))
+    U = rng.standard_normal((B, n))
+    if np.dtype(dtype).kind == "c":
+        A = A + 1j * rng.standard_normal((B, n, n))
+        U = U + 1j * rng.standard_normal((B, n))
+    S = (A - np.swapaxes(A, -1, -2)).astype(dtype)
+    U = U.astype(dtype)
+    idx = rng.integers(0, n, size=B)
+    G = 0.5 * np.swapaxes(np.linalg.inv(S), -1, -2)
+    s1, l1 = moves.pf_ratio_direct(S, U, idx)
+    r = moves.pf_ratio_woodbury(G, U, idx)
+    assert np.allclose(np.log(np.abs(r)), l1, rtol=0, atol=1e-9)
+    assert np.allclose(r / np.abs(r), s1, rtol=0, atol=1e-9)
+    G1 = moves.pf_grad_direct(S, U, idx)
+    assert np.abs(moves.pf_update_woodbury(G, U, idx) - G1).max() <= 1e-8 * np.abs(G1).max()
