@@ -65,9 +65,9 @@ def parse():
                     help="slogdet only: matrices are rows of a shared (SITES x n) phi picked by random occupations "
                          "(fermix_slogdet_gather, configuration 3's caller step); L2 flushed between timed steps")
     ap.add_argument("--move", type=int, default=0, metavar="K",
-                    help="time a k-row move instead: fermix_slogdet_update (ratio + in-place Woodbury update of "
-                         "G = A^-T) on the batch; G stays resident, e2e copies only the new rows / indices in and the "
-                         "ratio out")
+                    help="time a move instead: --op slogdet: fermix_slogdet_update (k-row ratio + in-place Woodbury "
+                         "update of G = A^-T); --op slogpf (K = 1): fermix_slogpf_update (one-index Pfaffian move on "
+                         "G = S^-T / 2). G stays resident; e2e copies only the new rows / indices in and the ratio out")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
@@ -329,24 +329,42 @@ def run_move(a, rank, world, local):
     rdt = torch.float32 if a.dtype in ("f32", "c64") else torch.float64
     kind = {"f32": 0, "f64": 1, "c64": 2, "c128": 3}[a.dtype]
     B, n, k = a.batch, a.n, a.move
+    pfm = a.op == "slogpf"
+    if pfm and (k != 1 or n % 2):
+        raise SystemExit("Pfaffian moves (--op slogpf) need --move 1 and an even n")
     gen = torch.Generator(device=dev)
     gen.manual_seed(a.seed + 1000 * rank)
-    # G of a well-conditioned A (identity-shifted); the moves replace random distinct rows by
-    # random rows near them, so every ratio stays O(1) while G is updated step after step
-    A = torch.randn((B, n, n), generator=gen, device=dev, dtype=tdt) / n**0.5 + 2 * torch.eye(n, device=dev)
-    G = torch.linalg.inv(A).transpose(-1, -2).contiguous()
-    IDX = torch.rand((B, n), generator=gen, device=dev).argsort(dim=1)[:, :k].to(torch.int32).contiguous()
+    # G of a well-conditioned matrix (identity-shifted A, or a skew S shifted by pair blocks
+    # [[0, 2], [-2, 0]]); the moves replace random rows by random rows near them, so every
+    # ratio stays O(1) while G is updated step after step
+    A = torch.randn((B, n, n), generator=gen, device=dev, dtype=tdt) / n**0.5
+    if pfm:
+        J = torch.zeros((n, n), device=dev, dtype=tdt)
+        r = torch.arange(0, n, 2, device=dev)
+        J[r, r + 1], J[r + 1, r] = 2.0, -2.0
+        A = A - A.transpose(-1, -2) + J
+        G = (0.5 * torch.linalg.inv(A).transpose(-1, -2)).contiguous()
+        IDX = torch.randint(0, n, (B, 1), generator=gen, device=dev, dtype=torch.int32)
+    else:
+        A = A + 2 * torch.eye(n, device=dev)
+        G = torch.linalg.inv(A).transpose(-1, -2).contiguous()
+        IDX = torch.rand((B, n), generator=gen, device=dev).argsort(dim=1)[:, :k].to(torch.int32).contiguous()
     U = (torch.gather(A, 1, IDX.long()[:, :, None].expand(B, k, n)) +
          0.1 * torch.randn((B, k, n), generator=gen, device=dev, dtype=tdt) / n**0.5).contiguous()
     del A
     sign = torch.empty(B, dtype=tdt, device=dev)
     logabs = torch.empty(B, dtype=rdt, device=dev)
-    wsb = L.fermix_slogdet_update_workspace_bytes(kind, B, n, k)
+    wsb = (L.fermix_slogpf_update_workspace_bytes(kind, B, n) if pfm else
+           L.fermix_slogdet_update_workspace_bytes(kind, B, n, k))
     ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
 
     def call(Ud, Id):
+        if pfm:
+            _lib.check(L.fermix_slogpf_update(sp, kind, B, n, G.data_ptr(), Ud.data_ptr(), Id.data_ptr(), None,
+                                              sign.data_ptr(), logabs.data_ptr(), ws.data_ptr(), wsb))
+            return
         _lib.check(L.fermix_slogdet_update(sp, kind, B, n, k, G.data_ptr(), Ud.data_ptr(), Id.data_ptr(), None,
                                            sign.data_ptr(), logabs.data_ptr(), ws.data_ptr(), wsb))
 
@@ -425,14 +443,18 @@ def run_move(a, rank, world, local):
         threads = os.cpu_count() or 1
         with threadpool_limits(limits=threads):
             t0 = time.perf_counter()
-            moves.ratio_woodbury(Gh, Uh, Ih)
-            moves.update_woodbury(Gh, Uh, Ih)
+            if pfm:
+                moves.pf_update_woodbury(Gh, Uh[:, 0], Ih[:, 0])
+            else:
+                moves.ratio_woodbury(Gh, Uh, Ih)
+                moves.update_woodbury(Gh, Uh, Ih)
             dt = time.perf_counter() - t0
         cpu = {"value": cnt / dt, "unit": "moves/s", "cores": threads, "kind": "port",
                "sample": f"{cnt} moves of the same workload ({dt:.2f} s; numpy Woodbury ratio + update in float64)"}
     if rank == 0:
         line = {
-            "metric": "k-row determinant moves/sec (ratio + in-place inverse update)",
+            "metric": ("one-index Pfaffian moves/sec (ratio + in-place gradient update)" if pfm else
+                       "k-row determinant moves/sec (ratio + in-place inverse update)"),
             "value": world * B * a.steps / t_dev,
             "unit": "moves/s",
             "n_gpus": world,
@@ -444,17 +466,19 @@ def run_move(a, rank, world, local):
             "vs_baseline": None,
             "dtype": a.dtype,
             "data": "synthetic (seeded G = inv(A)^T of A ~ N(0, 1/n) + 2I, new rows near the replaced ones)",
-            "config": {"workload": f"slogdet {k}-row move {a.dtype} B={B}/GPU n={n}", "op": "slogdet_update",
+            "config": {"workload": (f"slogpf one-index move {a.dtype} B={B}/GPU n={n}" if pfm else
+                                    f"slogdet {k}-row move {a.dtype} B={B}/GPU n={n}"),
+                       "op": "slogpf_update" if pfm else "slogdet_update",
                        "batch_per_gpu": B, "n": n, "k": k, "parallelism": f"batch sharded x{world}, no collective",
                        "l2": "G exceeds L2 (no flush needed)" if B * n * n * s > 126e6 else "G fits L2"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "upd_rows_vec_kernel",
+                         "kernel": "pfm_rows_kernel" if pfm else "upd_rows_vec_kernel",
                          "timing": "the whole call (ratio kernel + row kernel): an upper bound on the row kernel's time",
                          "algorithmic_bytes_per_launch": B * by},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": a.steps * 2,
+            "gpu_launches": a.steps * (3 if pfm else 2),
             "clocks": ck,
         }
         print(json.dumps(line), flush=True)

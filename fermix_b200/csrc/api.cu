@@ -746,6 +746,17 @@ int run_pf_move(cudaStream_t s, int64_t batch, int64_t n, void* g, const void* u
     p += align256((size_t)batch * n * sizeof(T));
     A.v = reinterpret_cast<T*>(p);
   }
+  if (apply && n * n * (int64_t)sizeof(T) <= kPfmSmemMax && (n * sizeof(T)) % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+    // G fits one block's shared memory: the whole move in one launch (the workspace is unused)
+    const size_t sm = pfm_smem_bytes((int)n, sizeof(T));
+    if (cudaFuncSetAttribute(pfm_smem_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) !=
+        cudaSuccess)
+      return FX_ERR_CUDA;
+    const int64_t cap = (int64_t)D->sms * 3;
+    pfm_smem_kernel<T><<<(unsigned)(batch < cap ? batch : cap), kPfmThreads, sm, s>>>(A);
+    return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+  }
   const int64_t wpb = kUpdRowThreads / 32, cap = (int64_t)D->sms * 8;
   const int64_t gp = (batch + wpb - 1) / wpb;
   pfm_prep_kernel<T><<<(unsigned)(gp < cap ? gp : cap), kUpdRowThreads, 0, s>>>(A);

@@ -25,6 +25,7 @@
 //   (the second read hits L1 / L2).
 #pragma once
 #include "scalar.cuh"
+#include "umma.cuh"
 
 namespace fx {
 
@@ -451,6 +452,108 @@ __global__ void __launch_bounds__(kUpdRowThreads) pfm_rows_kernel(PfMoveArgs<T> 
     }
   }
 }
+
+// Pfaffian move with G held in shared memory (n^2 s <= kPfmSmemMax bytes, n s a multiple of
+// 16): one block per matrix, the whole move in one launch. Thread 0 brings G in with one bulk
+// copy (cp.async.bulk, completing on an mbarrier; the wait is bounded and a timeout turns
+// the block's remaining outputs into NaN), then the ratio rho = 2 g_i . u, v = G u, y = e_i - 2v
+// and the updated rows (written straight to global) all read shared memory, so G crosses HBM
+// once each way: the 2 n^2 s roofline.
+constexpr int kPfmSmemMax = 64 * 1024;
+constexpr int kPfmThreads = 256;
+constexpr uint32_t kPfmWaitIters = 1u << 24;
+
+template <typename T>
+__global__ void __launch_bounds__(kPfmThreads) pfm_smem_kernel(PfMoveArgs<T> A) {
+  using R = typename Sc<T>::R;
+  extern __shared__ __align__(16) unsigned char pfm_raw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int NW = kPfmThreads / 32;
+  const int n = A.n;
+  T* Gs = reinterpret_cast<T*>(pfm_raw);  // n x n
+  T* us = Gs + (size_t)n * n;              // u with u_i = 0
+  T* ys = us + n;                          // y = e_i - 2 G u
+  T* red = ys + n;                         // red[NW]: the ratio
+  uint64_t* mbar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(red + NW + 1) + 7) & ~(uintptr_t)7);
+  __shared__ int s_dead, s_skip;
+  if (tid == 0) {
+    umma::mbar_init(mbar, 1);
+    umma::fence_mbar_init();
+    s_dead = 0;
+  }
+  __syncthreads();
+  uint32_t phase = 0;
+  const uint32_t bytes = (uint32_t)((size_t)n * n * sizeof(T));
+  for (int64_t b = blockIdx.x; b < A.B; b += gridDim.x) {
+    const int i = A.idx[b];
+    const bool bad = i < 0 || i >= n;
+    const bool acc = A.accept == nullptr || A.accept[b] != 0;
+    T* Gg = A.g + b * (int64_t)n * n;
+    const bool dead = s_dead != 0;
+    // rejected members need only the ratio (row i of G from global); the others load G
+    const bool load = !dead && !bad && acc;
+    if (load && tid == 0) {
+      umma::fence_proxy_async_smem();  // earlier generic reads of Gs before the async write
+      umma::mbar_arrive_expect_tx(mbar, bytes);
+      umma::bulk_g2s(Gs, Gg, bytes, mbar);
+    }
+    for (int c = tid; c < n; c += kPfmThreads) us[c] = (c == i || bad) ? s_zero<T>() : A.u[b * (int64_t)n + c];
+    if (load) {
+      if (!umma::mbar_wait(mbar, phase, kPfmWaitIters)) {
+        s_dead = 1;  // give the copy one more bounded wait; no later matrix loads into Gs
+        (void)umma::mbar_wait(mbar, phase, kPfmWaitIters);
+      }
+      phase ^= 1;
+    }
+    __syncthreads();
+    const bool fail = s_dead != 0;
+    // the ratio rho = 2 g_i . u by warp 0, in the order of pfm_prep_kernel (so that the
+    // ratio and update calls give the same bits)
+    const T* gi = load && !fail ? Gs + (size_t)i * n : Gg + (size_t)(bad ? 0 : i) * n;
+    T d = s_zero<T>();
+    if (warp == 0 && !bad && !fail) {
+      d = warp_dot_skip(gi, us, n, i, lane);
+      d = add(d, d);
+    }
+    if (tid == 0) {
+      const bool sing = !bad && is_zero(d);
+      A.sign[b] = (bad || fail) ? upd_nan<T>() : (sing ? s_zero<T>() : unit(d));
+      A.logabs[b] = (bad || fail) ? R(NAN) : (sing ? -R(INFINITY) : rlog(mag(d)));
+      red[NW] = d;
+      s_skip = (!load || fail) ? 1 : (sing ? 2 : 0);
+    }
+    __syncthreads();
+    const int skip = s_skip;
+    if (skip == 2) {  // accepted move with ratio exactly 0: G' = 0
+      for (int64_t e = tid; e < (int64_t)n * n; e += kPfmThreads) Gg[e] = s_zero<T>();
+    } else if (skip == 0) {
+      // y = e_i - 2 G u, one warp per row of the shared copy
+      for (int j = warp; j < n; j += NW) {
+        T acc2 = s_zero<T>();
+        for (int c = lane; c < n; c += 32) acc2 = fma_(Gs[(size_t)j * n + c], us[c], acc2);
+        acc2 = warp_sum_t<T>(acc2);
+        if (lane == 0) {
+          T yv = neg(add(acc2, acc2));
+          if (j == i) yv = add(yv, s_one<T>());
+          ys[j] = yv;
+        }
+      }
+      __syncthreads();
+      // G'_j = G_j + (y_j g_i - g_ij y) / rho
+      const T ri = recip(red[NW]);
+      const T* h = Gs + (size_t)i * n;
+      for (int j = warp; j < n; j += NW) {
+        const T c1 = mul(ys[j], ri), c2 = neg(mul(h[j], ri));
+        for (int c = lane; c < n; c += 32)
+          Gg[(size_t)j * n + c] = fma_(c2, ys[c], fma_(c1, h[c], Gs[(size_t)j * n + c]));
+      }
+    }
+    __syncthreads();  // Gs, us, ys, red free for the next matrix
+  }
+}
+
+// Gs, us, ys, red[9], then the mbarrier at the next 8-byte boundary
+inline size_t pfm_smem_bytes(int n, size_t s) { return (size_t)n * n * s + 2 * (size_t)n * s + 9 * s + 32; }
 
 // 16 bytes of consecutive elements: the unit of the vector row kernel
 template <typename T>
