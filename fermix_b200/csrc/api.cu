@@ -762,6 +762,23 @@ int run_pf_move(cudaStream_t s, int64_t batch, int64_t n, void* g, const void* u
   pfm_prep_kernel<T><<<(unsigned)(gp < cap ? gp : cap), kUpdRowThreads, 0, s>>>(A);
   if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
   if (apply) {
+    const size_t rowb = (size_t)n * sizeof(T);
+    const bool vec = rowb % 16 == 0 && rowb <= 8 * 512 &&
+                     ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u)) & 15) == 0;
+    if (vec) {
+      const int ch = rowb <= 512 ? 1 : rowb <= 1024 ? 2 : rowb <= 2048 ? 4 : 8;
+      const int rw = ch == 1 ? 4 : ch == 8 ? 1 : 2;
+      const int64_t need = (batch * ((n + rw - 1) / rw) + wpb - 1) / wpb;
+      const unsigned grid = (unsigned)(need < cap ? need : cap);
+      void* kv = ch == 1 ? (void*)&pfm_v_vec_kernel<T, 1, 4> : ch == 2 ? (void*)&pfm_v_vec_kernel<T, 2, 2>
+               : ch == 4 ? (void*)&pfm_v_vec_kernel<T, 4, 2> : (void*)&pfm_v_vec_kernel<T, 8, 1>;
+      void* kr = ch == 1 ? (void*)&pfm_rows_vec_kernel<T, 1, 4> : ch == 2 ? (void*)&pfm_rows_vec_kernel<T, 2, 2>
+               : ch == 4 ? (void*)&pfm_rows_vec_kernel<T, 4, 2> : (void*)&pfm_rows_vec_kernel<T, 8, 1>;
+      void* args[] = {&A};
+      if (cudaLaunchKernel(kv, dim3(grid), dim3(kUpdRowThreads), args, 0, s) != cudaSuccess) return FX_ERR_CUDA;
+      if (cudaLaunchKernel(kr, dim3(grid), dim3(kUpdRowThreads), args, 0, s) != cudaSuccess) return FX_ERR_CUDA;
+      return FX_OK;
+    }
     const int64_t gr = (batch * n + wpb - 1) / wpb;
     pfm_v_kernel<T><<<(unsigned)(gr < cap ? gr : cap), kUpdRowThreads, 0, s>>>(A);
     if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;

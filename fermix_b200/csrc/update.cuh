@@ -673,4 +673,117 @@ __global__ void __launch_bounds__(kUpdRowThreads, KM <= 4 ? 2 : 1) upd_rows_vec_
   }
 }
 
+// Vector forms of the Pfaffian move's two row passes (rows of up to 4 KB, a multiple of 16
+// bytes): RW rows of one matrix per warp as 16-byte pieces in registers, as upd_rows_vec_kernel.
+template <typename T, int CH, int RW>
+__global__ void __launch_bounds__(kUpdRowThreads, 2) pfm_v_vec_kernel(PfMoveArgs<T> A) {
+  constexpr int E = 16 / (int)sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int n = A.n, np = n / E, gpm = (n + RW - 1) / RW;
+  const int64_t groups = A.B * gpm;
+  const int64_t wstride = (int64_t)gridDim.x * (kUpdRowThreads / 32);
+  for (int64_t q = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5); q < groups; q += wstride) {
+    const int64_t b = q / gpm;
+    const int j0 = (int)(q - b * gpm) * RW;
+    if (A.act[b] != UPD_APPLY) continue;
+    const int i = A.idx[b];
+    const UpdPiece<T>* Gp = reinterpret_cast<const UpdPiece<T>*>(A.g + (b * n + j0) * (int64_t)n);
+    const UpdPiece<T>* Up = reinterpret_cast<const UpdPiece<T>*>(A.u + b * (int64_t)n);
+    T acc[RW];
+#pragma unroll
+    for (int w = 0; w < RW; ++w) acc[w] = s_zero<T>();
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int p = c * 32 + lane;
+      if (p < np) {
+        UpdPiece<T> u = Up[p];
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if (p * E + e == i) u.v[e] = s_zero<T>();  // u_i is not part of the move
+#pragma unroll
+        for (int w = 0; w < RW; ++w) {
+          if (j0 + w < n) {
+            const UpdPiece<T> x = Gp[(int64_t)w * np + p];
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[w] = fma_(u.v[e], x.v[e], acc[w]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int w = 0; w < RW; ++w) {
+      const T vj = warp_sum_t<T>(acc[w]);
+      if (lane == 0 && j0 + w < n) A.v[b * (int64_t)n + j0 + w] = vj;
+    }
+  }
+}
+
+template <typename T, int CH, int RW>
+__global__ void __launch_bounds__(kUpdRowThreads, 2) pfm_rows_vec_kernel(PfMoveArgs<T> A) {
+  constexpr int E = 16 / (int)sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int n = A.n, np = n / E, gpm = (n + RW - 1) / RW;
+  const int64_t groups = A.B * gpm;
+  const int64_t wstride = (int64_t)gridDim.x * (kUpdRowThreads / 32);
+  int64_t q = (int64_t)blockIdx.x * (kUpdRowThreads / 32) + (threadIdx.x >> 5);
+  int act_next = q < groups ? A.act[q / gpm] : UPD_KEEP;
+  for (; q < groups; q += wstride) {
+    const int64_t b = q / gpm;
+    const int j0 = (int)(q - b * gpm) * RW;
+    const int act = act_next;
+    if (q + wstride < groups) act_next = A.act[(q + wstride) / gpm];
+    if (act == UPD_KEEP) continue;
+    UpdPiece<T>* Gp = reinterpret_cast<UpdPiece<T>*>(A.g + (b * n + j0) * (int64_t)n);
+    if (act == UPD_ZERO) {
+      UpdPiece<T> z;
+#pragma unroll
+      for (int e = 0; e < E; ++e) z.v[e] = s_zero<T>();
+#pragma unroll
+      for (int w = 0; w < RW; ++w)
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+          if (c * 32 + lane < np && j0 + w < n) Gp[(int64_t)w * np + c * 32 + lane] = z;
+      continue;
+    }
+    const int i = A.idx[b];
+    const T* h = A.h + b * (int64_t)n;
+    const T* v = A.v + b * (int64_t)n;
+    const UpdPiece<T>* Hp = reinterpret_cast<const UpdPiece<T>*>(h);
+    const UpdPiece<T>* Vp = reinterpret_cast<const UpdPiece<T>*>(v);
+    const T ri = recip(A.rho[b]);
+    T c1[RW], c2[RW];
+#pragma unroll
+    for (int w = 0; w < RW; ++w) {
+      const int j = j0 + w < n ? j0 + w : j0;
+      T t = neg(add(v[j], v[j]));
+      if (j == i) t = add(t, s_one<T>());
+      c1[w] = mul(t, ri);            // (d_ij - 2 v_j) / rho
+      c2[w] = neg(mul(h[j], ri));    // -g_ij / rho
+    }
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int p = c * 32 + lane;
+      if (p < np) {
+        const UpdPiece<T> hp = Hp[p];
+        UpdPiece<T> y = Vp[p];
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          T t = neg(add(y.v[e], y.v[e]));
+          if (p * E + e == i) t = add(t, s_one<T>());
+          y.v[e] = t;  // y = e_i - 2 v
+        }
+#pragma unroll
+        for (int w = 0; w < RW; ++w) {
+          if (j0 + w < n) {
+            UpdPiece<T> x = Gp[(int64_t)w * np + p];
+#pragma unroll
+            for (int e = 0; e < E; ++e) x.v[e] = fma_(c2[w], y.v[e], fma_(c1[w], hp.v[e], x.v[e]));
+            Gp[(int64_t)w * np + p] = x;
+          }
+        }
+      }
+    }
+  }
+}
+
 }  // namespace fx
