@@ -678,10 +678,39 @@ int run_update(cudaStream_t s, int64_t batch, int64_t n, int64_t k, void* g, con
     const size_t rowb = (size_t)n * sizeof(T);
     const bool vec = rowb % 16 == 0 && rowb <= 8 * 512 &&
                      ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u)) & 15) == 0;
-    if (vec) {
+    const size_t blk_smem = 2 * (size_t)k * rowb;
+    if (vec && k > 1 && blk_smem <= (size_t)kUpdBlkSmem) {
+      // U and H of a matrix in shared memory, one block per matrix at a time
+      const int ch = rowb <= 512 ? 1 : rowb <= 1024 ? 2 : rowb <= 2048 ? 4 : 8;
+      const bool big = k > 4;
+      void* kern = nullptr;
+      if (big) {
+        kern = ch == 1 ? (sizeof(T) >= 8 ? (void*)&upd_rows_blk_kernel<T, 1, 1, kUpdMaxK>
+                                         : (void*)&upd_rows_blk_kernel<T, 1, 2, kUpdMaxK>)
+             : ch == 2 ? (void*)&upd_rows_blk_kernel<T, 2, 1, kUpdMaxK>
+             : ch == 4 ? (void*)&upd_rows_blk_kernel<T, 4, 1, kUpdMaxK>
+                       : (void*)&upd_rows_blk_kernel<T, 8, 1, kUpdMaxK>;
+      } else {
+        kern = ch == 1 ? (void*)&upd_rows_blk_kernel<T, 1, 2, 4>
+             : ch == 2 ? (void*)&upd_rows_blk_kernel<T, 2, 2, 4>
+             : ch == 4 ? (void*)&upd_rows_blk_kernel<T, 4, 1, 4>
+                       : (void*)&upd_rows_blk_kernel<T, 8, 1, 4>;
+      }
+      if (blk_smem > 48 * 1024 &&
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kUpdBlkSmem) != cudaSuccess)
+        return FX_ERR_CUDA;
+      const int64_t cap = (int64_t)D->sms * 4;
+      const unsigned grid = (unsigned)(batch < cap ? batch : cap);
+      void* args[] = {&A};
+      if (cudaLaunchKernel(kern, dim3(grid), dim3(kUpdRowThreads), args, blk_smem, s) != cudaSuccess)
+        return FX_ERR_CUDA;
+    } else if (vec) {
       // pieces per lane, and rows per warp: 4 KB of G in flight per warp where k <= 4
       const int ch = rowb <= 512 ? 1 : rowb <= 1024 ? 2 : rowb <= 2048 ? 4 : 8;
-      const int rw = k > 4 ? 1 : ch == 1 ? 4 : ch == 2 ? 2 : ch == 4 ? 2 : 1;
+      const bool k4 = k > 1 && k <= 4;
+      int rw = k > 4 ? 1 : ch == 1 ? 4 : ch == 2 ? 2 : ch == 4 ? 2 : 1;
+      if (k4 && ch == 1 && sizeof(T) >= 8) rw = 2;   // register budget of 4 coefficients per row
+      if (k4 && ch == 4 && sizeof(T) == 16) rw = 1;
       const int64_t need = (batch * ((n + rw - 1) / rw) + wpb - 1) / wpb;
       const unsigned grid = (unsigned)(need < rcap ? need : rcap);
       void* kern = nullptr;
@@ -691,9 +720,9 @@ int run_update(cudaStream_t s, int64_t batch, int64_t n, int64_t k, void* g, con
              : ch == 4 ? (void*)&upd_rows_vec_kernel<T, 4, 2, 1>
                        : (void*)&upd_rows_vec_kernel<T, 8, 1, 1>;
       } else if (k <= 4) {
-        kern = ch == 1 ? (void*)&upd_rows_vec_kernel<T, 1, 4, 4>
+        kern = ch == 1 ? (rw == 4 ? (void*)&upd_rows_vec_kernel<T, 1, 4, 4> : (void*)&upd_rows_vec_kernel<T, 1, 2, 4>)
              : ch == 2 ? (void*)&upd_rows_vec_kernel<T, 2, 2, 4>
-             : ch == 4 ? (void*)&upd_rows_vec_kernel<T, 4, 2, 4>
+             : ch == 4 ? (rw == 2 ? (void*)&upd_rows_vec_kernel<T, 4, 2, 4> : (void*)&upd_rows_vec_kernel<T, 4, 1, 4>)
                        : (void*)&upd_rows_vec_kernel<T, 8, 1, 4>;
       } else {
         kern = ch == 1 ? (void*)&upd_rows_vec_kernel<T, 1, 1, kUpdMaxK>

@@ -49,6 +49,12 @@ struct UpdArgs {
   int n, k;
 };
 
+// 16 bytes of consecutive elements: the unit of the vector row kernel
+template <typename T>
+struct alignas(16) UpdPiece {
+  T v[16 / sizeof(T)];
+};
+
 template <typename T>
 __device__ __forceinline__ void upd_swap(T& a, T& b) {
   const T t = a;
@@ -91,6 +97,39 @@ __device__ __forceinline__ c64_t warp_sum_t<c64_t>(c64_t v) {
 template <>
 __device__ __forceinline__ c128_t warp_sum_t<c128_t>(c128_t v) {
   return {warp_sum_t<double>(v.re), warp_sum_t<double>(v.im)};
+}
+
+template <typename T>
+__device__ __forceinline__ T upd_shfl_xor(T v, int m) {
+  if constexpr (Sc<T>::cx) {
+    v.re = __shfl_xor_sync(0xffffffffu, v.re, m);
+    v.im = __shfl_xor_sync(0xffffffffu, v.im, m);
+    return v;
+  } else {
+    return __shfl_xor_sync(0xffffffffu, v, m);
+  }
+}
+
+// Warp sums of KM per-lane partials (KM a power of two <= 16) at once: halving exchanges
+// over lane bits KM/2 .. 1 (the lane with the bit set keeps the upper half), then plain xor
+// sums over the remaining bits. Returns, in every lane, the full sum of index lane % KM;
+// (KM - 1) + (5 - log2 KM) shuffles instead of 5 KM. a is clobbered.
+template <typename T, int KM>
+__device__ __forceinline__ T warp_reduce_scatter(T (&a)[KM], int lane) {
+#pragma unroll
+  for (int half = KM / 2; half >= 1; half >>= 1) {
+    const bool up = (lane & half) != 0;
+#pragma unroll
+    for (int t = 0; t < half; ++t) {
+      const T send = up ? a[t] : a[t + half];
+      const T keep = up ? a[t + half] : a[t];
+      a[t] = add(keep, upd_shfl_xor<T>(send, half));
+    }
+  }
+  T v = a[0];
+#pragma unroll
+  for (int o = KM; o < 32; o <<= 1) v = add(v, upd_shfl_xor<T>(v, o));
+  return v;
 }
 
 // x . y over n entries: lane partials in column order, then the xor tree (every lane
@@ -340,6 +379,108 @@ __global__ void __launch_bounds__(kUpdRowThreads) upd_rows_kernel(UpdArgs<T> A) 
   }
 }
 
+// k > 1 with U and H of a matrix staged in shared memory (2 k n s <= kUpdBlkSmem bytes): one
+// block per matrix at a time; its warps sweep the matrix's rows RW at a time, reading U and H
+// from shared memory instead of once per row from L2.
+constexpr int kUpdBlkSmem = 100 * 1024;  // two blocks per SM
+
+template <typename T, int CH, int RW, int KM>
+__global__ void __launch_bounds__(kUpdRowThreads, 2) upd_rows_blk_kernel(UpdArgs<T> A) {
+  constexpr int E = 16 / (int)sizeof(T);
+  constexpr int NWP = kUpdRowThreads / 32;
+  extern __shared__ __align__(16) unsigned char upd_raw[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = A.n, k = A.k, np = n / E;
+  UpdPiece<T>* Us = reinterpret_cast<UpdPiece<T>*>(upd_raw);  // k x np
+  UpdPiece<T>* Hs = Us + (size_t)k * np;                       // k x np
+  __shared__ int ids[kUpdMaxK];
+  for (int64_t b = blockIdx.x; b < A.B; b += gridDim.x) {
+    const int act = A.act[b];
+    if (act == UPD_KEEP) continue;  // block-uniform
+    UpdPiece<T>* Gp = reinterpret_cast<UpdPiece<T>*>(A.g + b * (int64_t)n * n);
+    if (act == UPD_ZERO) {
+      UpdPiece<T> z;
+#pragma unroll
+      for (int e = 0; e < E; ++e) z.v[e] = s_zero<T>();
+      for (int64_t e = tid; e < (int64_t)n * np; e += kUpdRowThreads) Gp[e] = z;
+      continue;
+    }
+    const UpdPiece<T>* Up = reinterpret_cast<const UpdPiece<T>*>(A.u + b * (int64_t)k * n);
+    const UpdPiece<T>* Hp = reinterpret_cast<const UpdPiece<T>*>(A.h + b * (int64_t)k * n);
+    for (int e = tid; e < k * np; e += kUpdRowThreads) {
+      Us[e] = Up[e];
+      Hs[e] = Hp[e];
+    }
+    if (tid < k) ids[tid] = A.idx[b * k + tid];
+    __syncthreads();
+    for (int j0 = warp * RW; j0 < n; j0 += NWP * RW) {
+      UpdPiece<T> x[RW][CH];
+#pragma unroll
+      for (int w = 0; w < RW; ++w)
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          const int p = c * 32 + lane;
+          if (p < np && j0 + w < n) {
+            x[w][c] = Gp[(int64_t)(j0 + w) * np + p];
+          } else {
+#pragma unroll
+            for (int e = 0; e < E; ++e) x[w][c].v[e] = s_zero<T>();
+          }
+        }
+      T cf[RW][KM];
+#pragma unroll
+      for (int w = 0; w < RW; ++w)
+#pragma unroll
+        for (int r = 0; r < KM; ++r) cf[w][r] = s_zero<T>();
+#pragma unroll
+      for (int r = 0; r < KM; ++r) {
+        if (r < k) {
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
+            const int p = c * 32 + lane;
+            if (p < np) {
+              const UpdPiece<T> u = Us[r * np + p];
+#pragma unroll
+              for (int e = 0; e < E; ++e)
+#pragma unroll
+                for (int w = 0; w < RW; ++w) cf[w][r] = fma_(u.v[e], x[w][c].v[e], cf[w][r]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int w = 0; w < RW; ++w) {
+        const T tot = warp_reduce_scatter<T, KM>(cf[w], lane);
+#pragma unroll
+        for (int r = 0; r < KM; ++r) cf[w][r] = shfl_idx<T>(tot, r);
+#pragma unroll
+        for (int r = 0; r < KM; ++r)
+          if (r < k && ids[r] == j0 + w) cf[w][r] = sub(cf[w][r], s_one<T>());
+      }
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int p = c * 32 + lane;
+        if (p < np) {
+#pragma unroll
+          for (int r = 0; r < KM; ++r) {
+            if (r < k) {
+              const UpdPiece<T> h = Hs[r * np + p];
+#pragma unroll
+              for (int w = 0; w < RW; ++w)
+#pragma unroll
+                for (int e = 0; e < E; ++e) x[w][c].v[e] = fms(x[w][c].v[e], cf[w][r], h.v[e]);
+            }
+          }
+#pragma unroll
+          for (int w = 0; w < RW; ++w)
+            if (j0 + w < n) Gp[(int64_t)(j0 + w) * np + p] = x[w][c];
+        }
+      }
+    }
+    __syncthreads();  // Us, Hs, ids free for the next matrix
+  }
+}
+
 // ---------------------------------------------------------------- Pfaffian moves (k = 1)
 // A one-electron move of a Pfaffian wavefunction replaces row and column i of the skew S by
 // u and -u (u_i is ignored: the skew diagonal stays 0). The state is the slogpf gradient
@@ -555,12 +696,6 @@ __global__ void __launch_bounds__(kPfmThreads) pfm_smem_kernel(PfMoveArgs<T> A) 
 // Gs, us, ys, red[9], then the mbarrier at the next 8-byte boundary
 inline size_t pfm_smem_bytes(int n, size_t s) { return (size_t)n * n * s + 2 * (size_t)n * s + 9 * s + 32; }
 
-// 16 bytes of consecutive elements: the unit of the vector row kernel
-template <typename T>
-struct alignas(16) UpdPiece {
-  T v[16 / sizeof(T)];
-};
-
 // CH: 16-byte pieces per lane (row bytes <= CH * 512); RW: rows per warp; KM: the largest k
 template <typename T, int CH, int RW, int KM>
 __global__ void __launch_bounds__(kUpdRowThreads, KM <= 4 ? 2 : 1) upd_rows_vec_kernel(UpdArgs<T> A) {
@@ -612,13 +747,15 @@ __global__ void __launch_bounds__(kUpdRowThreads, KM <= 4 ? 2 : 1) upd_rows_vec_
             }
           }
       }
+      // lane partials of the k dot products of each row, then one reduce-scatter per row
       T cf[RW][KM];
+#pragma unroll
+      for (int w = 0; w < RW; ++w)
+#pragma unroll
+        for (int r = 0; r < KM; ++r) cf[w][r] = s_zero<T>();
 #pragma unroll
       for (int r = 0; r < KM; ++r) {
         if (r < k) {
-          T acc[RW];
-#pragma unroll
-          for (int w = 0; w < RW; ++w) acc[w] = s_zero<T>();
 #pragma unroll
           for (int c = 0; c < CH; ++c) {
             const int p = c * 32 + lane;
@@ -627,17 +764,23 @@ __global__ void __launch_bounds__(kUpdRowThreads, KM <= 4 ? 2 : 1) upd_rows_vec_
 #pragma unroll
               for (int e = 0; e < E; ++e)
 #pragma unroll
-                for (int w = 0; w < RW; ++w) acc[w] = fma_(u.v[e], x[w][c].v[e], acc[w]);
+                for (int w = 0; w < RW; ++w) cf[w][r] = fma_(u.v[e], x[w][c].v[e], cf[w][r]);
             }
           }
-          const int ir = __ldg(id + r);
-#pragma unroll
-          for (int w = 0; w < RW; ++w) {
-            T v = warp_sum_t<T>(acc[w]);
-            if (ir == j0 + w) v = sub(v, s_one<T>());
-            cf[w][r] = v;
-          }
         }
+      }
+#pragma unroll
+      for (int w = 0; w < RW; ++w) {
+        if constexpr (KM == 1) {
+          cf[w][0] = warp_sum_t<T>(cf[w][0]);
+        } else {
+          const T tot = warp_reduce_scatter<T, KM>(cf[w], lane);  // the sum of index lane % KM
+#pragma unroll
+          for (int r = 0; r < KM; ++r) cf[w][r] = shfl_idx<T>(tot, r);
+        }
+#pragma unroll
+        for (int r = 0; r < KM; ++r)
+          if (r < k && __ldg(id + r) == j0 + w) cf[w][r] = sub(cf[w][r], s_one<T>());
       }
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
