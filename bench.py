@@ -59,7 +59,8 @@ def parse():
     ap.add_argument("--dtype", default="f32", choices=["f32", "f64", "c64", "c128"])
     ap.add_argument("--prec", default="tf32x3", choices=["tf32x3", "ieee"])
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--cpu-sample", type=int, default=256, help="matrices in the CPU baseline sample")
+    ap.add_argument("--cpu-sample", type=int, default=1536,
+                    help="matrices in the CPU baseline sample (about 10-20 s of host work at the default workload)")
     ap.add_argument("--ref-step", type=int, default=16, help="matrices per step of the reference arm")
     ap.add_argument("--gather", type=int, default=0, metavar="SITES",
                     help="slogdet only: matrices are rows of a shared (SITES x n) phi picked by random occupations "
