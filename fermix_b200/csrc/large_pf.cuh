@@ -20,6 +20,7 @@
 //      mirrored (the update S += tau w^T - w tau^T keeps S exactly skew).
 #pragma once
 #include "large_lu.cuh"
+#include "umma.cuh"
 
 namespace fx {
 

@@ -1,0 +1,11 @@
+// Register-panel and generic one-block-per-matrix kernels for float32 / float64.
+#include "launch_fused.inl"
+
+namespace fxh {
+#define FXH_INST(T)                                                               \
+  template int plan_fused<T, false>(int64_t, int, int, Plan&);                    \
+  template int plan_fused<T, true>(int64_t, int, int, Plan&);                     \
+  template int launch_fused<T, false>(cudaStream_t, Job<T>, void*, size_t);       \
+  template int launch_fused<T, true>(cudaStream_t, Job<T>, void*, size_t);
+FXH_FOR_REAL(FXH_INST)
+}  // namespace fxh

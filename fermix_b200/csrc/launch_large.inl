@@ -1,0 +1,220 @@
+// Blocked engines for n > 256 (large_lu.cuh, large_pf.cuh): workspace layout, batch
+// slices and the host-side panel loops. Included by launch_large_real.cu and
+// launch_large_complex.cu, which instantiate it for their dtypes.
+#pragma once
+#include "dispatch.cuh"
+#include "large_pf.cuh"
+
+namespace fxh {
+
+// ---------------------------------------------------------------- large-n LU engine
+// n > kSmallMax, slogdet forward and gradient: the panel loop of large_lu.cuh over slices
+// of the batch. Workspace per matrix: the matrix itself, the panel coefficients and
+// pivot-row snapshot, L11 / U11, pivots and index arrays; each array 256-byte aligned.
+constexpr int kLgSliceBlocks = 4;  // a slice holds at most SMs x 4 matrices
+
+template <typename T>
+struct LgLayout {
+  size_t M, C, P, LU, piv, ipiv, cand, perm, flag, total;
+  LgLayout(int64_t bs, int n) {
+    constexpr int NB = LgCfg<T>::NB;
+    const int nchunk = (n + kLgChunk - 1) / kLgChunk;
+    size_t o = 0;
+    M = o;    o = align256(o + (size_t)bs * n * n * sizeof(T));
+    C = o;    o = align256(o + (size_t)bs * n * NB * sizeof(T));
+    P = o;    o = align256(o + (size_t)bs * NB * n * sizeof(T));
+    LU = o;   o = align256(o + (size_t)bs * 3 * NB * NB * sizeof(T));
+    piv = o;  o = align256(o + (size_t)bs * n * sizeof(T));
+    ipiv = o; o = align256(o + (size_t)bs * n * sizeof(int));
+    cand = o; o = align256(o + (size_t)bs * nchunk * NB * sizeof(int));
+    perm = o; o = align256(o + (size_t)bs * n * sizeof(int));
+    flag = o; o = align256(o + (size_t)bs * sizeof(int));
+    total = o;
+  }
+};
+
+constexpr size_t kLgSliceBytes = (size_t)8 << 30;  // workspace aimed at per slice (8 GiB)
+
+// Matrices per slice: enough to fill the GPU (SMs x 4), no more than the batch, and the
+// workspace kept near kLgSliceBytes for large n (at least one matrix).
+template <typename T>
+int64_t lg_slice(int64_t batch, int n) {
+  const DevInfo* D = dev_info();
+  int64_t cap = (int64_t)(D ? D->sms : 148) * kLgSliceBlocks;
+  const int64_t by_mem = (int64_t)(kLgSliceBytes / LgLayout<T>(1, n).total);
+  if (by_mem < cap) cap = by_mem < 1 ? 1 : by_mem;
+  return batch < cap ? batch : cap;
+}
+
+template <typename T>
+size_t lg_ws_bytes(int64_t batch, int n) {
+  return LgLayout<T>(lg_slice<T>(batch, n), n).total;
+}
+
+template <typename T>
+int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool pf_grad) {
+  constexpr int NB = LgCfg<T>::NB;
+  const int n = J.n;
+  if (!ws) return FX_ERR_WORKSPACE;
+  int64_t bs = lg_slice<T>(J.B, n);
+  while (bs > 1 && LgLayout<T>(bs, n).total > wsb) bs = bs / 2;
+  const LgLayout<T> Lw(bs, n);
+  if (Lw.total > wsb) return FX_ERR_WORKSPACE;
+  unsigned char* w = static_cast<unsigned char*>(ws);
+  LgArgs<T> A{};
+  A.M = reinterpret_cast<T*>(w + Lw.M);
+  A.C = reinterpret_cast<T*>(w + Lw.C);
+  A.P = reinterpret_cast<T*>(w + Lw.P);
+  A.LU11 = reinterpret_cast<T*>(w + Lw.LU);
+  A.piv = reinterpret_cast<T*>(w + Lw.piv);
+  A.ipiv = reinterpret_cast<int*>(w + Lw.ipiv);
+  A.cand = reinterpret_cast<int*>(w + Lw.cand);
+  A.perm = reinterpret_cast<int*>(w + Lw.perm);
+  A.flag = reinterpret_cast<int*>(w + Lw.flag);
+  A.n = n;
+  A.grad = grad ? 1 : 0;
+  A.primal = pf_grad ? 0 : 1;
+  A.gscale = pf_grad ? typename Sc<T>::R(0.5) : typename Sc<T>::R(1);
+  A.zsign = pf_grad ? J.sign : nullptr;
+  const size_t leaf_smem = kLgChunk * sizeof(int) + lg_gepp_smem<T>();
+  const size_t tree_smem = lg_tree_smem<T>((n + kLgChunk - 1) / kLgChunk);
+  void* tree_k = (void*)&lg_tree_kernel<T>;
+  if (tree_smem > 48 * 1024 &&
+      cudaFuncSetAttribute(tree_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tree_smem) != cudaSuccess)
+    return FX_ERR_CUDA;
+  for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
+    const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);
+    if (pf_grad && J.skew) {
+      lg_skew_copy_kernel<T><<<dim3((n + 31) / 32, (n + 31) / 32, cnt), 256, 0, s>>>(A.M, J.a + b0 * (int64_t)n * n, n);
+    } else if (cudaMemcpyAsync(A.M, J.a + b0 * (int64_t)n * n, (size_t)cnt * n * n * sizeof(T),
+                               cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+      return FX_ERR_CUDA;
+    }
+    for (int k0 = 0; k0 < n; k0 += NB) {
+      A.k0 = k0;
+      A.kw = n - k0 < NB ? n - k0 : NB;
+      A.nchunk = (n - k0 + kLgChunk - 1) / kLgChunk;
+      if (A.nchunk > 1) lg_leaf_kernel<T><<<dim3(A.nchunk, cnt), kLgChunk, leaf_smem, s>>>(A);
+      lg_tree_kernel<T><<<cnt, kLgChunk, tree_smem, s>>>(A);
+      const int c_lo = grad ? 0 : k0;
+      lg_swap_kernel<T><<<dim3((n - c_lo + 255) / 256, cnt), 256, 0, s>>>(A, c_lo);
+      const int r_lo = grad ? 0 : k0;
+      if (grad) {
+        lg_coef_kernel<T, true><<<dim3((n - r_lo + 255) / 256, cnt), 256, 0, s>>>(A, r_lo);
+      } else {
+        lg_coef_kernel<T, false><<<dim3((n - r_lo + 255) / 256, cnt), 256, 0, s>>>(A, r_lo);
+      }
+      const int u_lo = grad ? 0 : k0 + A.kw;
+      if (u_lo < n) lg_update_kernel<T><<<dim3((n - u_lo + 63) / 64, (n - u_lo + 63) / 64, cnt), 256, 0, s>>>(A, u_lo, u_lo);
+    }
+    lg_finish_kernel<T><<<cnt, 32, 0, s>>>(A, J, b0, grad ? 1 : 0);
+    if (grad) {
+      lg_check_kernel<T><<<dim3(16, cnt), 256, 0, s>>>(A);
+      lg_grad_kernel<T><<<dim3((n + 31) / 32, (n + 31) / 32, cnt), 256, 0, s>>>(A, J, b0);
+    }
+    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  }
+  return FX_OK;
+}
+
+// Cluster launch of the split panel: CL blocks of 1024 threads per matrix.
+template <typename T, int CL>
+int launch_pfl_cl(cudaStream_t s, const PflArgs<T>& A, int cnt) {
+  const size_t smem = pfl_panel_cl_smem<T>();
+  void* k = (void*)&pfl_panel_cl_kernel<T, CL>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return FX_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(CL * cnt));
+  cfg.blockDim = dim3(kPflRows);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CL;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  PflArgs<T> arg = A;
+  void* args[] = {&arg};
+  return cudaLaunchKernelExC(&cfg, k, args) == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+}
+
+// Large-n Parlett-Reid forward (kSmallMax < n <= kPflMaxN, n even): the panel loop of
+// large_pf.cuh over slices of the batch, on the large-LU workspace layout.
+template <typename T>
+int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
+  constexpr int NP = PflCfg<T>::NP;
+  const int n = J.n;
+  if (!ws) return FX_ERR_WORKSPACE;
+  int64_t bs = lg_slice<T>(J.B, n);
+  while (bs > 1 && LgLayout<T>(bs, n).total > wsb) bs = bs / 2;
+  const LgLayout<T> Lw(bs, n);
+  if (Lw.total > wsb) return FX_ERR_WORKSPACE;
+  unsigned char* w = static_cast<unsigned char*>(ws);
+  PflArgs<T> A{};
+  A.M = reinterpret_cast<T*>(w + Lw.M);
+  A.C = reinterpret_cast<T*>(w + Lw.C);
+  A.P = reinterpret_cast<T*>(w + Lw.P);
+  A.dvec = reinterpret_cast<T*>(w + Lw.piv);
+  A.ipiv = reinterpret_cast<int*>(w + Lw.ipiv);
+  A.n = n;
+  LgArgs<T> U{};
+  U.M = A.M;
+  U.C = A.C;
+  U.P = A.P;
+  U.n = n;
+  // n <= 512: 512-row panel blocks with twice the pairs (a wider, less memory-bound update)
+  const bool small = n <= 512;
+  constexpr int NPS = PflCfg<T>::NP_SMALL;
+  const int np_max = small ? NPS : NP;
+  const size_t psmem = small ? pfl_panel_smem<T, NPS, 512>() : pfl_panel_smem<T, NP, kPflRows>();
+  void* pk = small ? (void*)&pfl_panel_kernel<T, NPS, 512> : (void*)&pfl_panel_kernel<T, NP, kPflRows>;
+  if (cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) != cudaSuccess)
+    return FX_ERR_CUDA;
+  for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
+    const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);
+    if (J.skew) {
+      lg_skew_copy_kernel<T><<<dim3((n + 31) / 32, (n + 31) / 32, cnt), 256, 0, s>>>(A.M, J.a + b0 * (int64_t)n * n, n);
+    } else if (cudaMemcpyAsync(A.M, J.a + b0 * (int64_t)n * n, (size_t)cnt * n * n * sizeof(T),
+                               cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+      return FX_ERR_CUDA;
+    }
+    for (int k0 = 0; k0 < n; k0 += 2 * np_max) {
+      A.k0 = k0;
+      A.np = (n - k0) / 2 < np_max ? (n - k0) / 2 : np_max;
+      const int m = n - k0;
+      if (small) {
+        pfl_panel_kernel<T, NPS, 512><<<cnt, 512, psmem, s>>>(A);
+      } else if (m <= kPflRows) {
+        pfl_panel_kernel<T, NP, kPflRows><<<cnt, kPflRows, psmem, s>>>(A);
+      } else {
+        int e = FX_ERR_SHAPE;
+        switch ((m + kPflRows - 1) / kPflRows) {
+          case 2: e = launch_pfl_cl<T, 2>(s, A, cnt); break;
+          case 3: e = launch_pfl_cl<T, 3>(s, A, cnt); break;
+          case 4: e = launch_pfl_cl<T, 4>(s, A, cnt); break;
+          case 5: e = launch_pfl_cl<T, 5>(s, A, cnt); break;
+          case 6: e = launch_pfl_cl<T, 6>(s, A, cnt); break;
+          case 7: e = launch_pfl_cl<T, 7>(s, A, cnt); break;
+          case 8: e = launch_pfl_cl<T, 8>(s, A, cnt); break;
+        }
+        if (e) return e;
+      }
+      pfl_swap_rows_kernel<T><<<dim3((n - k0 + 255) / 256, cnt), 256, 0, s>>>(A);
+      pfl_swap_cols_kernel<T><<<dim3((n - k0 + 255) / 256, cnt), 256, 0, s>>>(A);
+      const int lo = k0 + 2 * A.np;
+      if (lo < n) {
+        U.k0 = k0;
+        U.kw = 2 * A.np;
+        lg_update_kernel<T, true><<<dim3((n - lo + 63) / 64, (n - lo + 63) / 64, cnt), 256, 0, s>>>(U, lo, lo);
+      }
+    }
+    pfl_finish_kernel<T><<<cnt, 32, 0, s>>>(A, J, b0);
+    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  }
+  return FX_OK;
+}
+
+}  // namespace fxh

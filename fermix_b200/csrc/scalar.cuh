@@ -287,7 +287,7 @@ struct KSum {
 // Optional per-phase cycle counters for profiling builds (-DFX_PHASE_TIMERS): thread 0
 // of each block adds clock64() deltas into fx_phase_cycles[phase].
 #ifdef FX_PHASE_TIMERS
-__device__ unsigned long long fx_phase_cycles[16];
+static __device__ unsigned long long fx_phase_cycles[16];
 #define FX_TIC(var) long long var = clock64()
 #define FX_TOC(var, ph)                                                              \
   do {                                                                               \
