@@ -15,6 +15,8 @@ LIB_PATH = os.path.join(LIB_DIR, "libfermix_b200.so")
 FX_F32, FX_F64, FX_C64, FX_C128 = 0, 1, 2, 3
 FX_PREC_DEFAULT, FX_PREC_TF32X3, FX_PREC_IEEE = 0, 1, 2
 FX_OP_SLOGDET, FX_OP_SLOGPF = 0, 1
+FX_ERR_TIMEOUT = 8
+FX_WAIT_POLLS_DEFAULT = 1 << 26
 
 # every symbol include/fermix_b200.h declares, with its ctypes signature
 _vp, _i, _i64, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
@@ -38,6 +40,8 @@ SIGNATURES = {
     "fermix_strerror": (ctypes.c_char_p, [_i]),
     "fermix_version": (_i, []),
     "fermix_selftest_umma": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp]),
+    "fermix_device_status": (_i, [_i]),
+    "fermix_set_wait_polls": (ctypes.c_uint, [ctypes.c_uint]),
 }
 
 _lib = None
@@ -67,6 +71,13 @@ def lib():
                 fn.argtypes = args
             _lib = h
     return _lib
+
+
+def device_status(clear=False):
+    """The kernels' status on the current CUDA device (synchronises it): 0, or
+    FX_ERR_TIMEOUT when a kernel gave up a bounded wait since the last clear (its members'
+    outputs are NaN). Entry points are stream-ordered, so they cannot return it."""
+    return lib().fermix_device_status(int(clear))
 
 
 def check(status):

@@ -250,83 +250,127 @@ class _GradKernel(torch.autograd.Function):
         return G.reshape((V,) + rest + (n, n)), 0
 
 
+# Derivative matrices (B, n, n) up to this many bytes are computed by the forward launch
+# and kept for the backward, so that one factorisation serves both (the reference's rule,
+# src/fermix/_diff.py:111-124). Larger ones are not kept: the backward factorises again,
+# which holds no (B, n, n) residual between the passes.
+KEEP_GRAD_BYTES = 8 << 30
+
+
+def _keep(A):
+    """Whether the forward should also produce the derivative matrix for the backward."""
+    return (torch.is_grad_enabled() and A.requires_grad and
+            A.numel() * A.element_size() <= KEEP_GRAD_BYTES)
+
+
+def _scale_grad(D, c):
+    """The gradient conj(c * D) from the kept derivative matrix D (torch's complex
+    convention; the same product the kernels form when given coef and conj_out)."""
+    G = c.to(D.dtype)[:, None, None] * D
+    return torch.conj(G) if D.is_complex() else G
+
+
 class _Slog(torch.autograd.Function):
     """(sign, logabs) of slogdet (op=SLOGDET) or slogpf (op=SLOGPF) on a (B, n, n)
-    batch. Backward re-runs the factorisation with the gradient epilogue (one fused
-    launch writing the scaled gradient), so no (B, n, n) residual is kept; the primal it
-    recomputes is bit-identical to the forward's."""
+    batch. With keep (the input requires grad and the derivative fits KEEP_GRAD_BYTES) the
+    forward is one launch of the fused factorisation + gradient kernel, whose primal is
+    bit-identical to the forward kernel's, and the backward scales the kept derivative;
+    otherwise the backward re-runs the factorisation with the gradient epilogue."""
 
     @staticmethod
-    def forward(A, op, prec, skew):
+    def forward(A, op, prec, skew, keep):
+        if keep:
+            sign, logabs, _, D = _run(op, A, prec, skew=skew, grad=True)
+            return sign, logabs, D
         sign, logabs, _ = _FwdKernel.apply(A, op, prec, skew)
-        return sign, logabs
+        return sign, logabs, None
 
     @staticmethod
     def setup_context(ctx, inputs, output):
-        A, op, prec, skew = inputs
-        ctx.save_for_backward(A, output[0])
-        ctx.save_for_forward(A, output[0])
+        A, op, prec, skew, keep = inputs
+        D = output[2]
+        if D is not None:
+            ctx.mark_non_differentiable(D)
+        ctx.save_for_backward(A, output[0], D)
+        ctx.save_for_forward(A, output[0], D)
         ctx.op, ctx.prec, ctx.skew = op, prec, skew
 
     @staticmethod
-    def backward(ctx, g_sign, g_logabs):
-        A, sign = ctx.saved_tensors
+    def backward(ctx, g_sign, g_logabs, _g_d):
+        A, sign, D = ctx.saved_tensors
         c = _slog_coef(sign, g_sign, g_logabs, A.is_complex())
+        if D is not None:
+            return _scale_grad(D, c), None, None, None, None
         G = _GradKernel.apply(A, c, ctx.op, ctx.prec, ctx.skew, True, False)
-        return G, None, None, None
+        return G, None, None, None, None
 
     @staticmethod
     def jvp(ctx, dA, *_):
-        A, sign = ctx.saved_tensors
-        D = _GradKernel.apply(A, None, ctx.op, ctx.prec, ctx.skew, False, False)
+        A, sign, D = ctx.saved_tensors
+        if D is None:
+            D = _GradKernel.apply(A, None, ctx.op, ctx.prec, ctx.skew, False, False)
         t = (D * dA).sum(dim=(-1, -2))
         if A.is_complex():
-            return (1j * t.imag).to(sign.dtype) * sign, t.real
-        return torch.zeros_like(sign), t
+            return (1j * t.imag).to(sign.dtype) * sign, t.real, None
+        return torch.zeros_like(sign), t, None
 
     @staticmethod
-    def vmap(info, in_dims, A, op, prec, skew):
+    def vmap(info, in_dims, A, op, prec, skew, keep):
         if in_dims[0] is None:
-            return _Slog.apply(A, op, prec, skew), (None, None)
+            return _Slog.apply(A, op, prec, skew, keep), (None, None, None)
         X, V, rest = _fold(A, in_dims[0])
-        out = _Slog.apply(X, op, prec, skew)
-        return tuple(o.reshape((V,) + rest) for o in out), (0, 0)
+        s, l, D = _Slog.apply(X, op, prec, skew, keep)
+        n = X.shape[-1]
+        out = (s.reshape((V,) + rest), l.reshape((V,) + rest), None if D is None else D.reshape((V,) + rest + (n, n)))
+        return out, (0, 0, None if D is None else 0)
 
 
 class _Value(torch.autograd.Function):
     """det (op=SLOGDET) or pf (op=SLOGPF) value on a (B, n, n) batch, with the
-    singular-safe adjugate gradient."""
+    singular-safe adjugate gradient (kept from the forward launch under the same rule as
+    _Slog)."""
 
     @staticmethod
-    def forward(A, op, prec, skew):
-        return _FwdKernel.apply(A, op, prec, skew)[2]
+    def forward(A, op, prec, skew, keep):
+        if keep:
+            _, _, val, D = _run(op, A, prec, skew=skew, grad=True, adjugate=True, value=True)
+            return val, D
+        return _FwdKernel.apply(A, op, prec, skew)[2], None
 
     @staticmethod
     def setup_context(ctx, inputs, output):
-        A, op, prec, skew = inputs
-        ctx.save_for_backward(A)
-        ctx.save_for_forward(A)
+        A, op, prec, skew, keep = inputs
+        D = output[1]
+        if D is not None:
+            ctx.mark_non_differentiable(D)
+        ctx.save_for_backward(A, D)
+        ctx.save_for_forward(A, D)
         ctx.op, ctx.prec, ctx.skew = op, prec, skew
 
     @staticmethod
-    def backward(ctx, g):
-        (A,) = ctx.saved_tensors
+    def backward(ctx, g, _g_d):
+        A, D = ctx.saved_tensors
         c = torch.conj(g) if A.is_complex() else g
+        if D is not None:
+            return _scale_grad(D, c), None, None, None, None
         G = _GradKernel.apply(A, c, ctx.op, ctx.prec, ctx.skew, True, True)
-        return G, None, None, None
+        return G, None, None, None, None
 
     @staticmethod
     def jvp(ctx, dA, *_):
-        (A,) = ctx.saved_tensors
-        D = _GradKernel.apply(A, None, ctx.op, ctx.prec, ctx.skew, False, True)
-        return (D * dA).sum(dim=(-1, -2))
+        A, D = ctx.saved_tensors
+        if D is None:
+            D = _GradKernel.apply(A, None, ctx.op, ctx.prec, ctx.skew, False, True)
+        return (D * dA).sum(dim=(-1, -2)), None
 
     @staticmethod
-    def vmap(info, in_dims, A, op, prec, skew):
+    def vmap(info, in_dims, A, op, prec, skew, keep):
         if in_dims[0] is None:
-            return _Value.apply(A, op, prec, skew), None
+            return _Value.apply(A, op, prec, skew, keep), (None, None)
         X, V, rest = _fold(A, in_dims[0])
-        return _Value.apply(X, op, prec, skew).reshape((V,) + rest), 0
+        v, D = _Value.apply(X, op, prec, skew, keep)
+        n = X.shape[-1]
+        return (v.reshape((V,) + rest), None if D is None else D.reshape((V,) + rest + (n, n))), (0, None if D is None else 0)
 
 
 # ------------------------------------------------------------------ public functions
@@ -552,7 +596,7 @@ def slogdet(a, *, prec=None, unroll_steps=None, block=None):
     _check_unroll(unroll_steps)
     p = _check_prec(a.dtype, prec)
     A, batch, n = _flat(a)
-    sign, logabs = _Slog.apply(A, _lib.FX_OP_SLOGDET, p, True)
+    sign, logabs, _ = _Slog.apply(A, _lib.FX_OP_SLOGDET, p, True, _keep(a))
     return sign.reshape(batch), logabs.reshape(batch)
 
 
@@ -565,7 +609,7 @@ def slogpf(a, *, prec=None, skew_symmetrize=True, upd_warps=None):
     _check_upd_warps(upd_warps)
     p = _check_prec(a.dtype, prec)
     A, batch, n = _flat(a)
-    sign, logabs = _Slog.apply(A, _lib.FX_OP_SLOGPF, p, bool(skew_symmetrize))
+    sign, logabs, _ = _Slog.apply(A, _lib.FX_OP_SLOGPF, p, bool(skew_symmetrize), _keep(a))
     return sign.reshape(batch), logabs.reshape(batch)
 
 
@@ -578,7 +622,7 @@ def det(a, *, prec=None, unroll_steps=None, block=None):
     _check_unroll(unroll_steps)
     p = _check_prec(a.dtype, prec)
     A, batch, n = _flat(a)
-    return _Value.apply(A, _lib.FX_OP_SLOGDET, p, True).reshape(batch)
+    return _Value.apply(A, _lib.FX_OP_SLOGDET, p, True, _keep(a))[0].reshape(batch)
 
 
 def pf(a, *, prec=None, skew_symmetrize=True, upd_warps=None):
@@ -589,7 +633,7 @@ def pf(a, *, prec=None, skew_symmetrize=True, upd_warps=None):
     _check_upd_warps(upd_warps)
     p = _check_prec(a.dtype, prec)
     A, batch, n = _flat(a)
-    return _Value.apply(A, _lib.FX_OP_SLOGPF, p, bool(skew_symmetrize)).reshape(batch)
+    return _Value.apply(A, _lib.FX_OP_SLOGPF, p, bool(skew_symmetrize), _keep(a))[0].reshape(batch)
 
 
 # ------------------------------------------------------------------ one-launch parts

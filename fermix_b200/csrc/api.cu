@@ -7,9 +7,11 @@
 //                                 fused_pf.cuh): work buffers in shared memory when
 //                                 they fit (227 KB per block on B200), else in the
 //                                 caller's workspace (one slot per resident block).
-// The only process state is a once-initialised per-device attribute cache.
+// Process state: a once-initialised per-device attribute cache, the bounded-wait limit
+// (fermix_set_wait_polls) and the device address of the static scratch array.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -39,11 +41,40 @@ int validate(int dtype, int prec, int64_t batch, int64_t n) {
   return fermix_check_prec(dtype, prec);
 }
 
+static std::atomic<uint32_t> g_wait_polls{FX_WAIT_POLLS_DEFAULT};
+
+uint32_t wait_polls() { return g_wait_polls.load(std::memory_order_relaxed); }
+
 }  // namespace fxh
 
 namespace {
 
 using namespace fxh;
+
+static_assert(FX_ERR_TIMEOUT == 8, "the kernels record FX_ERR_TIMEOUT as 8");
+
+// The kernels cut the workspace into 256-byte aligned arrays and read some of them as
+// 16-byte pieces. A caller's workspace of any alignment is therefore moved up to the next
+// 256-byte boundary here; the *_workspace_bytes queries include those 256 bytes.
+constexpr size_t kWsSlack = 256;
+
+void align_workspace(void*& ws, size_t& wsb) {
+  if (!ws) {
+    wsb = 0;
+    return;
+  }
+  const uintptr_t p = reinterpret_cast<uintptr_t>(ws);
+  const size_t skip = (size_t)(((p + 255) & ~(uintptr_t)255) - p);
+  if (wsb <= skip) {
+    ws = nullptr;
+    wsb = 0;
+    return;
+  }
+  ws = reinterpret_cast<void*>(p + skip);
+  wsb -= skip;
+}
+
+size_t with_slack(size_t bytes) { return bytes ? bytes + kWsSlack : 0; }
 
 template <typename T>
 int launch_poly(cudaStream_t s, const Job<T>& J, int is_pf) {
@@ -250,6 +281,7 @@ int fermix_slogdet(void* stream, int dtype, int prec, int64_t batch, int64_t n, 
   if (e) return e;
   if (batch == 0) return FX_OK;
   if ((!a && n > 0) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
@@ -265,6 +297,7 @@ int fermix_slogdet_grad(void* stream, int dtype, int prec, int64_t batch, int64_
   if (e) return e;
   if (batch == 0) return FX_OK;
   if ((!a && n > 0) || !sign || !logabs || (!grad && n > 0)) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
   return by_dtype(dtype, [&](auto t) {
@@ -279,6 +312,7 @@ int fermix_slogpf(void* stream, int dtype, int prec, int64_t batch, int64_t n, i
   if (e) return e;
   if (batch == 0) return FX_OK;
   if ((!a && n > 0) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
@@ -294,6 +328,7 @@ int fermix_slogpf_grad(void* stream, int dtype, int prec, int64_t batch, int64_t
   if (e) return e;
   if (batch == 0) return FX_OK;
   if ((!a && n > 0) || !sign || !logabs || (!grad && n > 0)) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
   return by_dtype(dtype, [&](auto t) {
@@ -312,6 +347,7 @@ int fermix_slogdet_gather(void* stream, int dtype, int prec, int64_t batch, int6
   if (phi_rows < 0 || phi_ld < n) return FX_ERR_SHAPE;
   if (batch == 0) return FX_OK;
   if ((n > 0 && (!phi || !occ)) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
@@ -322,20 +358,20 @@ int fermix_slogdet_gather(void* stream, int dtype, int prec, int64_t batch, int6
 
 size_t fermix_slogdet_gather_workspace_bytes(int dtype, int prec, int64_t batch, int64_t n, int grad) {
   if (validate(dtype, prec, batch, n) || batch == 0) return 0;
-  return (size_t)by_dtype(dtype, [&](auto t) -> int {
+  return with_slack((size_t)by_dtype(dtype, [&](auto t) -> int {
     using T = decltype(t);
     return (int)((gather_ws_bytes<T>(prec, batch, n, grad) + 255) / 256);
-  }) * 256;
+  }) * 256);
 }
 
 size_t fermix_workspace_bytes(int op, int dtype, int64_t batch, int64_t n, int grad) {
   if (validate(dtype, FX_PREC_DEFAULT, batch, n) || batch == 0) return 0;
-  return (size_t)by_dtype(dtype, [&](auto t) -> int {
+  // returned through an int-typed dispatcher: counted in 256-byte units
+  const size_t units = (size_t)by_dtype(dtype, [&](auto t) -> int {
     using T = decltype(t);
-    size_t b = ws_bytes_t<T>(op, batch, n, grad);
-    // returned through an int-typed dispatcher: report in 256-byte units
-    return (int)((b + 255) / 256);
-  }) * 256;
+    return (int)((ws_bytes_t<T>(op, batch, n, grad) + 255) / 256);
+  });
+  return with_slack(units * 256);
 }
 
 const char* fermix_strerror(int code) {
@@ -356,11 +392,23 @@ const char* fermix_strerror(int code) {
       return "CUDA launch or attribute call failed";
     case FX_ERR_DEVICE:
       return "no usable CUDA device";
+    case FX_ERR_TIMEOUT:
+      return "a bounded wait inside a kernel gave up; the affected members' outputs are NaN";
   }
   return "unknown error code";
 }
 
-int fermix_version(void) { return 100; }
+int fermix_version(void) { return 200; }
+
+unsigned fermix_set_wait_polls(unsigned polls) { return g_wait_polls.exchange(polls); }
+
+int fermix_device_status(int clear) {
+  if (!dev_info()) return FX_ERR_DEVICE;
+  if (cudaDeviceSynchronize() != cudaSuccess) return FX_ERR_CUDA;
+  const int a = tc_status(clear), b = update_status(clear);
+  if (a < 0 || b < 0) return FX_ERR_CUDA;
+  return a ? a : b;
+}
 
 int fermix_slogpf_ratio(void* stream, int dtype, int64_t batch, int64_t n, const void* g, const void* row,
                         const int* idx, void* sign, void* logabs) {
@@ -384,6 +432,7 @@ int fermix_slogpf_update(void* stream, int dtype, int64_t batch, int64_t n, void
   if (n < 2) return FX_ERR_SHAPE;
   if (batch == 0) return FX_OK;
   if (!g || !row || !idx || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
@@ -393,10 +442,10 @@ int fermix_slogpf_update(void* stream, int dtype, int64_t batch, int64_t n, void
 
 size_t fermix_slogpf_update_workspace_bytes(int dtype, int64_t batch, int64_t n) {
   if (validate(dtype, FX_PREC_DEFAULT, batch, n) || batch == 0 || n < 2) return 0;
-  return (size_t)by_dtype(dtype, [&](auto t) -> int {
+  return with_slack((size_t)by_dtype(dtype, [&](auto t) -> int {
     using T = decltype(t);
     return (int)((pfm_ws_bytes<T>(batch, n) + 255) / 256);
-  }) * 256;
+  }) * 256);
 }
 
 int fermix_slogdet_ratio(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, const void* g,
@@ -420,6 +469,7 @@ int fermix_slogdet_update(void* stream, int dtype, int64_t batch, int64_t n, int
   if (e) return e;
   if (batch == 0) return FX_OK;
   if ((k > 0 && (!g || !rows || !idx)) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
@@ -429,10 +479,10 @@ int fermix_slogdet_update(void* stream, int dtype, int64_t batch, int64_t n, int
 
 size_t fermix_slogdet_update_workspace_bytes(int dtype, int64_t batch, int64_t n, int64_t k) {
   if (upd_validate(dtype, batch, n, k) || batch == 0) return 0;
-  return (size_t)by_dtype(dtype, [&](auto t) -> int {
+  return with_slack((size_t)by_dtype(dtype, [&](auto t) -> int {
     using T = decltype(t);
     return (int)((upd_ws_bytes<T>(batch, n, k) + 255) / 256);
-  }) * 256;
+  }) * 256);
 }
 
 }  // extern "C"
@@ -453,26 +503,30 @@ static __device__ __align__(256) unsigned char fx_static_scratch[FX_STATIC_SCRAT
 
 namespace {
 
-void* g_scratch_ptr[kMaxDevices];
-std::once_flag g_scratch_once[kMaxDevices];
+std::atomic<void*> g_scratch_ptr[kMaxDevices];
+std::mutex g_scratch_mu;
 
-// Device address of fx_static_scratch on the current device, looked up once per device
-// with that device current (nullptr if the lookup failed). The lookup may load this
-// module on the device, so the first call on each device belongs before any stream
-// capture.
+// Device address of fx_static_scratch on the current device, looked up with that device
+// current on the first call that succeeds (nullptr if the lookup failed). Only a
+// successful lookup is kept: a failed one is tried again on the next call. The lookup may
+// load this module on the device, so the first call on each device belongs before any
+// stream capture.
 void* static_scratch() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::call_once(g_scratch_once[dev], [dev]() {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, fx_static_scratch) == cudaSuccess) {
-      g_scratch_ptr[dev] = p;
-    } else {
-      g_scratch_ptr[dev] = nullptr;
-      (void)cudaGetLastError();  // clear the error state so later calls report their own errors
-    }
-  });
-  return g_scratch_ptr[dev];
+  void* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (p) return p;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (p) return p;
+  // an error the caller had already left pending is not ours to clear
+  const bool clean = cudaPeekAtLastError() == cudaSuccess;
+  if (cudaGetSymbolAddress(&p, fx_static_scratch) != cudaSuccess) {
+    if (clean) (void)cudaGetLastError();  // clear only the error this lookup set
+    return nullptr;
+  }
+  g_scratch_ptr[dev].store(p, std::memory_order_release);
+  return p;
 }
 
 }  // namespace
@@ -487,7 +541,8 @@ int fermix_slogdet_grad_static(void* stream, int dtype, int prec, int64_t batch,
   if (batch == 0) return FX_OK;
   if ((!a && n > 0) || !sign || !logabs || (!grad && n > 0)) return FX_ERR_NULL;
   // one matrix slot must fit: the workspace a single-member batch needs is one slot
-  const size_t slot = fermix_workspace_bytes(FX_OP_SLOGDET, dtype, 1, n, 1);
+  size_t slot = fermix_workspace_bytes(FX_OP_SLOGDET, dtype, 1, n, 1);
+  if (slot) slot -= kWsSlack;  // the array is 256-byte aligned: no alignment slack needed
   if (slot > (size_t)FX_STATIC_SCRATCH_BYTES) return FX_ERR_WORKSPACE;
   void* scratch = static_scratch();
   if (!scratch) return FX_ERR_CUDA;

@@ -39,6 +39,15 @@ const DevInfo* dev_info();
 
 int validate(int dtype, int prec, int64_t batch, int64_t n);
 
+// Polls of each bounded wait for launches issued now (fermix_set_wait_polls).
+uint32_t wait_polls();
+
+// Status word of one translation unit's kernels on the current device (0 or an FX_ERR_*
+// code), reset to 0 when clear; -1 if it cannot be read. Defined in launch_tc.cu and
+// launch_update.cu, the files whose kernels have bounded waits.
+int tc_status(int clear);
+int update_status(int clear);
+
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 constexpr int kSmallMax = 256;  // register-panel kernels: ceil(n / 32) <= 8 rows per lane
@@ -66,6 +75,7 @@ Job<T> make_job(int64_t batch, int64_t n, const void* a, const void* coef, int c
   J.B = batch;
   J.n = (int)n;
   J.mode = mode;
+  J.wait_polls = wait_polls();
   return J;
 }
 

@@ -46,6 +46,7 @@ struct Job {
   int ld;                      // leading dimension of the work buffers
   int in_smem;                 // work buffers in dynamic shared memory
   T* ws;                       // global work slots (gridDim.x * nbuf * n * ld) otherwise
+  uint32_t wait_polls;         // polls of each bounded wait (tensor-memory kernels)
   // row gather (tensor-memory LU only): matrix b row i = gbase[gidx[b * n + i] * gld + 0 .. n),
   // NaN for an index outside [0, grows)
   const int* gidx;

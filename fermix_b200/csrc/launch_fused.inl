@@ -48,7 +48,9 @@ int plan_fused(int64_t batch, int n, int mode, Plan& P) {
     P.kernel = small_kernel_ptr<T, PF>(rows_per_lane(n));
   else
     P.kernel = PF ? (void*)&pf_fused_kernel<T> : (void*)&lu_fused_kernel<T>;
-  if (cudaFuncSetAttribute(P.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem) != cudaSuccess)
+  // the device's opt-in limit, the same value on every call: one kernel serves a range of
+  // n, and a per-call size could be lowered by a concurrent call between set and launch
+  if (cudaFuncSetAttribute(P.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, D->smem_optin) != cudaSuccess)
     return FX_ERR_CUDA;
   // shared memory over L1: these kernels keep their matrices in shared memory
   if (cudaFuncSetAttribute(P.kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)

@@ -80,7 +80,7 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
   const size_t tree_smem = lg_tree_smem<T>((n + kLgChunk - 1) / kLgChunk);
   void* tree_k = (void*)&lg_tree_kernel<T>;
   if (tree_smem > 48 * 1024 &&
-      cudaFuncSetAttribute(tree_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tree_smem) != cudaSuccess)
+      cudaFuncSetAttribute(tree_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (dev_info() ? dev_info()->smem_optin : (int)tree_smem)) != cudaSuccess)
     return FX_ERR_CUDA;
   for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
     const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);

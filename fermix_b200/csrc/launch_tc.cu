@@ -60,6 +60,16 @@ int launch_lu_tc(cudaStream_t s, Job<float> J) {
   return FX_OK;
 }
 
+int tc_status(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, umma::fx_status_word, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(umma::fx_status_word, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+
 }  // namespace fxh
 
 extern "C" {

@@ -141,6 +141,7 @@ int run_pf_move(cudaStream_t s, int64_t batch, int64_t n, void* g, const void* u
   A.act = nullptr;
   A.B = batch;
   A.n = (int)n;
+  A.wait_polls = wait_polls();
   if (apply) {
     if (!ws || wsb < pfm_ws_bytes<T>(batch, n)) return FX_ERR_WORKSPACE;
     unsigned char* p = static_cast<unsigned char*>(ws);
@@ -156,7 +157,10 @@ int run_pf_move(cudaStream_t s, int64_t batch, int64_t n, void* g, const void* u
       (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
     // G fits one block's shared memory: the whole move in one launch (the workspace is unused)
     const size_t sm = pfm_smem_bytes((int)n, sizeof(T));
-    if (cudaFuncSetAttribute(pfm_smem_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) !=
+    // the limit is one constant bound for every n this path takes (n^2 s <= kPfmSmemMax), so
+    // concurrent calls with different n on other host threads all write the same value
+    if (cudaFuncSetAttribute(pfm_smem_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(kPfmSmemMax + 4096)) !=
         cudaSuccess)
       return FX_ERR_CUDA;
     const int64_t cap = (int64_t)D->sms * 3;
@@ -192,6 +196,16 @@ int run_pf_move(cudaStream_t s, int64_t batch, int64_t n, void* g, const void* u
     if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
   }
   return FX_OK;
+}
+
+int update_status(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, umma::fx_status_word, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(umma::fx_status_word, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
 }
 
 #define FXH_INST(T)                                                                                       \

@@ -375,7 +375,13 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
           umma::mma_commit(&S.mbar);
         }
         __syncwarp();
-        if (!umma::mbar_wait(&S.mbar, phase, kTcWaitIters)) S.bad = 1;
+        if (!umma::mbar_wait(&S.mbar, phase, J.wait_polls)) {
+          // give up on this member (NaN outputs, the status word records the timeout), but
+          // wait once more, with the default limit, so that no MMA is still in flight when
+          // the threads touch its operands, TMEM or the tensor memory allocation again
+          S.bad = 1;
+          (void)umma::mbar_wait(&S.mbar, phase, kTcWaitIters);
+        }
         phase ^= 1;
         umma::fence_after_sync();
       }
@@ -414,7 +420,8 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
         const float la = nz ? -INFINITY : lsum;
         J.sign[b] = S.bad ? __int_as_float(0x7fc00000) : sg;
         J.logabs[b] = S.bad ? __int_as_float(0x7fc00000) : la;
-        if (J.value) J.value[b] = sg * expf(la);
+        if (J.value) J.value[b] = S.bad ? __int_as_float(0x7fc00000) : sg * expf(la);
+        if (S.bad) umma::record_status(8);  // FX_ERR_TIMEOUT
         S.nz = nz;
       }
     }

@@ -134,8 +134,16 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
       : "memory");
 }
 
+// Status word of the kernels in one translation unit (each .cu file that includes this
+// header has its own copy, read back by that file's status function): 0, or the first
+// error code a kernel recorded (8 = FX_ERR_TIMEOUT, a bounded wait that gave up).
+static __device__ int fx_status_word;
+
+__device__ __forceinline__ void record_status(int code) { atomicCAS(&fx_status_word, 0, code); }
+
 // Wait for the phase with the given parity to complete; gives up after max_iters polls
-// and returns false (the caller records an error instead of hanging).
+// and returns false (the caller records an error instead of hanging). max_iters == 0
+// gives up at once.
 __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint32_t max_iters) {
   const uint32_t a = smem_u32(mbar);
   for (uint32_t it = 0; it < max_iters; ++it) {

@@ -504,6 +504,7 @@ struct PfMoveArgs {
   int* act;                     // (B,) workspace: UPD_KEEP / UPD_APPLY / UPD_ZERO
   int64_t B;
   int n;
+  uint32_t wait_polls;          // polls of the bounded copy wait (pfm_smem_kernel)
 };
 
 // x . y over n entries with entry `skip` left out
@@ -640,7 +641,7 @@ __global__ void __launch_bounds__(kPfmThreads) pfm_smem_kernel(PfMoveArgs<T> A) 
     }
     for (int c = tid; c < n; c += kPfmThreads) us[c] = (c == i || bad) ? s_zero<T>() : A.u[b * (int64_t)n + c];
     if (load) {
-      if (!umma::mbar_wait(mbar, phase, kPfmWaitIters)) {
+      if (!umma::mbar_wait(mbar, phase, A.wait_polls)) {
         s_dead = 1;  // give the copy one more bounded wait; no later matrix loads into Gs
         (void)umma::mbar_wait(mbar, phase, kPfmWaitIters);
       }
@@ -662,6 +663,7 @@ __global__ void __launch_bounds__(kPfmThreads) pfm_smem_kernel(PfMoveArgs<T> A) 
       A.logabs[b] = (bad || fail) ? R(NAN) : (sing ? -R(INFINITY) : rlog(mag(d)));
       red[NW] = d;
       s_skip = (!load || fail) ? 1 : (sing ? 2 : 0);
+      if (fail) umma::record_status(8);  // FX_ERR_TIMEOUT: G is left as it was
     }
     __syncthreads();
     const int skip = s_skip;

@@ -58,6 +58,7 @@ extern "C" {
 #define FX_ERR_NULL 5      /* a required pointer is NULL */
 #define FX_ERR_CUDA 6      /* a CUDA launch / attribute call failed */
 #define FX_ERR_DEVICE 7    /* no usable CUDA device */
+#define FX_ERR_TIMEOUT 8   /* a bounded wait inside a kernel gave up (reported by fermix_device_status) */
 
 /* (sign, logabs) of each matrix; value = sign * exp(logabs) (det) or, for n <= 4, the
  * explicit polynomial. value may be NULL. Replaces _slogdet_core / _lu_core. */
@@ -169,6 +170,23 @@ size_t fermix_slogpf_update_workspace_bytes(int dtype, int64_t batch, int64_t n)
 int fermix_slogdet_grad_static(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a,
                                const void* coef, int conj_out, int adjugate, void* sign, void* logabs, void* value,
                                void* grad);
+
+/* Status of the library's kernels on the current device (no reference counterpart):
+ * FX_OK, or FX_ERR_TIMEOUT when a kernel gave up one of its bounded waits (a tensor-core
+ * completion or a bulk copy that did not arrive) since the status was last cleared. The
+ * members such a kernel was working on got NaN outputs; the kernel waited once more, with
+ * the default limit, for the operation in flight before it released tensor memory and
+ * returned, so the context stays usable. Entry points are stream-ordered and cannot
+ * return this code themselves. This call synchronises the device first; clear != 0 resets
+ * the status to FX_OK. Returns FX_ERR_CUDA / FX_ERR_DEVICE if the status cannot be read. */
+int fermix_device_status(int clear);
+
+/* Polls of each bounded wait in the library's kernels, for launches issued after the call
+ * (process-wide; no reference counterpart). FX_WAIT_POLLS_DEFAULT is the default; 0 makes
+ * every such wait give up at once, which tests of the timeout path use. Returns the
+ * previous value. */
+#define FX_WAIT_POLLS_DEFAULT (1u << 26)
+unsigned fermix_set_wait_polls(unsigned polls);
 
 /* Workspace bytes a call needs on the current device (0 when every matrix fits in one
  * block's shared memory); grad != 0 for the *_grad entry points. */

@@ -43,9 +43,10 @@ def test_check_prec_and_strerror(lib):
     assert lib.fermix_check_prec(_lib.FX_F64, _lib.FX_PREC_TF32X3) == 3
     assert lib.fermix_check_prec(_lib.FX_C128, _lib.FX_PREC_TF32X3) == 3
     assert lib.fermix_check_prec(_lib.FX_F32, 9) == 3
-    for code in range(8):
+    for code in range(9):
         assert lib.fermix_strerror(code)
-    assert lib.fermix_version() >= 100
+        assert lib.fermix_strerror(code) != b"unknown error code"
+    assert lib.fermix_version() >= 200
 
 
 def test_argument_errors_before_any_device_work(lib):

@@ -55,6 +55,19 @@ def _relerr(x, ref):
 @pytest.mark.parametrize("dtype", DTYPES, ids=IDS)
 @pytest.mark.parametrize("n,k", [(1, 1), (8, 1), (33, 3), (128, 1), (128, 4), (300, 16)])
 def test_ratio_and_update_match_refactorisation(dtype, n, k):
+    _ratio_and_update(dtype, n, k)
+
+
+@pytest.mark.parametrize("dtype,n,k", [
+    (np.float32, 1024, 16),  # the register row kernel with 16 coefficients (U, H beyond shared memory)
+    (np.float32, 128, 3),    # shared-memory row kernel, k not a power of two (padded coefficients)
+    (np.float64, 128, 7),    # as above, 16 coefficient slots
+], ids=["f32-n1024-k16", "f32-n128-k3", "f64-n128-k7"])
+def test_row_kernel_variants_match_refactorisation(dtype, n, k):
+    _ratio_and_update(dtype, n, k)
+
+
+def _ratio_and_update(dtype, n, k):
     B = 6
     A, G, U, idx = _case(dtype, B, n, k, seed=n * 17 + k)
     s, l = fx.slogdet_ratio(cuda(G), cuda(U), cuda(idx))
