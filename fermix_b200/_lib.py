@@ -42,6 +42,9 @@ SIGNATURES = {
     "fermix_selftest_umma": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp]),
     "fermix_device_status": (_i, [_i]),
     "fermix_set_wait_polls": (ctypes.c_uint, [ctypes.c_uint]),
+    # include/fermix_b200_xla.h
+    "fermix_xla_custom_call": (None, [_vp, _vp, ctypes.c_char_p, _sz]),
+    "fermix_xla_last_error": (_i, [_i]),
 }
 
 _lib = None
