@@ -69,15 +69,27 @@ def parse():
                     help="time a move instead: --op slogdet: fermix_slogdet_update (k-row ratio + in-place Woodbury "
                          "update of G = A^-T); --op slogpf (K = 1): fermix_slogpf_update (one-index Pfaffian move on "
                          "G = S^-T / 2). G stays resident; e2e copies only the new rows / indices in and the ratio out")
+    ap.add_argument("--planar", action="store_true",
+                    help="complex dtypes: inputs and gradients as split real / imaginary planes (fermix_*_planar)")
+    ap.add_argument("--cpu-n", type=int, default=0,
+                    help="time the CPU baseline at this n instead (for sizes where the restatement takes minutes)")
+    ap.add_argument("--per-config", default="auto", choices=["auto", "on", "off"],
+                    help="add a per_config array (every BASELINE configuration) to the line; auto: on for the "
+                         "default workload at N = 1")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    return ap.parse_args()
+    a = ap.parse_args()
+    d = ap.parse_args([])
+    a.is_default = all(getattr(a, k) == getattr(d, k) for k in
+                       ("op", "fwd_only", "batch", "n", "dtype", "prec", "gather", "move", "planar"))
+    return a
 
 
 def workload_name(a):
     what = "fwd" if a.fwd_only else "fwd+VJP(logabs)"
     g = f" gathered from phi {a.gather}x{a.n}" if a.gather else ""
-    return f"{a.op} {what} {a.dtype} B={a.batch}/GPU n={a.n} prec={a.prec}{g}"
+    p = " planar" if getattr(a, "planar", False) and a.dtype in ("c64", "c128") else ""
+    return f"{a.op} {what} {a.dtype}{p} B={a.batch}/GPU n={a.n} prec={a.prec}{g}"
 
 
 def flops_bytes(a):
@@ -94,66 +106,6 @@ def flops_bytes(a):
         # the shared phi once per launch, the occupations, and the gradient written
         by = a.gather * n * s / a.batch + n * 4 + (0 if a.fwd_only else n * n * s)
     return fl * cx, by
-
-
-# FMA-pipe peaks measured on this pool's B200s at 1965 MHz (8 independent FMA chains per
-# thread, 148 x 8 blocks of 256 threads, CUDA events)
-FFMA_TFLOPS = 72.6
-DFMA_TFLOPS = 34.1
-
-
-def compute_roofline(a, flops_per_launch, launch_s):
-    """The arithmetic pipe that bounds this workload and the fraction of it achieved:
-    the tensor cores for the tensor-memory kernels (TF32 at half the measured bf16 rate,
-    divided by the TF32 products per update), the FP32 / FP64 FMA pipes otherwise."""
-    kern = kernel_name(a)
-    achieved = flops_per_launch / launch_s / 1e12
-    if kern in TC_KERNEL.values():
-        p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-        bf16 = float(json.load(open(p))["bf16_tflops"]) if os.path.exists(p) else 1590.0
-        products = 4 if a.op == "slogdet" else 3
-        pipe, peak = f"tcgen05 kind::tf32, {products} products per update", 0.5 * bf16 / products
-    elif a.dtype in ("f32", "c64"):
-        pipe, peak = "fp32 FFMA", FFMA_TFLOPS
-    else:
-        pipe, peak = "fp64 DFMA", DFMA_TFLOPS
-    return {"pipe": pipe, "achieved_tflops": achieved, "peak_tflops": peak, "frac": achieved / peak}
-
-
-def launches_per_call(a, sms=148):
-    """Kernels one library call launches for this workload, mirroring the dispatch of
-    fermix_b200/csrc/api.cu: one for n <= 256 (odd-n slogpf, the closed forms, the
-    tensor-memory and register-panel kernels); for n > 256 the blocked engines' kernels per
-    panel and per batch slice (a slice: at most SMs x 4 matrices and about 8 GiB)."""
-    n, B = a.n, a.batch
-    if n <= 256 or (a.op == "slogpf" and n % 2):
-        return 1
-    s = {"f32": 4, "f64": 8, "c64": 8, "c128": 16}[a.dtype]
-    nb = 32 if s <= 8 else 16
-    per_mat = n * n * s + 2 * n * nb * s + 3 * nb * nb * s + n * s + 3 * n * 4 + ((n + 511) // 512) * nb * 4
-    bs = max(1, min(B, sms * 4, (8 << 30) // per_mat))
-    slices = (B + bs - 1) // bs
-    grad = not a.fwd_only
-
-    def lu_engine():
-        k = 0
-        for k0 in range(0, n, nb):
-            kw = min(nb, n - k0)
-            k += (1 if (n - k0 + 511) // 512 > 1 else 0) + 3 + (1 if (grad or k0 + kw < n) else 0)
-        return k + 1 + (2 if grad else 0)
-
-    if a.op == "slogdet":
-        return slices * lu_engine()
-    # slogpf: the skew copy, per panel the panel kernel, two swaps and the update, the finish
-    npair = (nb // 2) if n <= 512 else (8 if s <= 8 else 4)
-    k = 1
-    for k0 in range(0, n, 2 * npair):
-        np_ = min(npair, (n - k0) // 2)
-        k += 3 + (1 if k0 + 2 * np_ < n else 0)
-    k += 1
-    if grad:
-        k += 1 + lu_engine()  # the skew copy of the gradient engine, then the LU engine
-    return slices * k
 
 
 def peaks():
@@ -488,41 +440,161 @@ def run_move(a, rank, world, local):
         dist.destroy_process_group()
 
 
-# --------------------------------------------------------------- GPU arm
-def main():
-    a = parse()
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if a.impl == "reference":
-        run_reference(a, rank)
-        return
-    if a.move:
-        run_move(a, rank, world, local)
-        return
+# --------------------------------------------------------------- measured pipe peaks
+_PIPES = {}
 
-    import numpy as np
+
+def pipe_peaks(dev):
+    """Arithmetic peaks measured on this GPU (TFLOP/s), once per process: the FP32 / FP64
+    FMA pipes with the library's FMA-throughput probe (fermix_selftest_fma_rate: 148 x 8
+    blocks of 256 threads, 8 independent chains each), and TF32 tensor throughput as
+    cuBLAS fp32 matmul with TF32 enabled (8192^3, best of 5)."""
+    if _PIPES:
+        return _PIPES
     import torch
 
     from fermix_b200 import _lib
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    out = torch.empty(4096, dtype=torch.float64, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks, iters = sms * 8, 1 << 14
+    for name, kind in (("ffma", _lib.FX_F32), ("dfma", _lib.FX_F64)):
+        best = None
+        for _ in range(4):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            _lib.check(L.fermix_selftest_fma_rate(stream.cuda_stream, kind, blocks, iters, out.data_ptr()))
+            e1.record(stream)
+            e1.synchronize()
+            t = e0.elapsed_time(e1) / 1e3
+            best = t if best is None else min(best, t)
+        _PIPES[name] = blocks * 256 * 16.0 * iters / best / 1e12
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        a = torch.randn((8192, 8192), device=dev)
+        b = torch.randn((8192, 8192), device=dev)
+        torch.matmul(a, b)
+        best = None
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            torch.matmul(a, b)
+            e1.record(stream)
+            e1.synchronize()
+            t = e0.elapsed_time(e1) / 1e3
+            best = t if best is None else min(best, t)
+        _PIPES["tf32"] = 2 * 8192.0**3 / best / 1e12
+        del a, b
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return _PIPES
 
-        import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+def compute_roofline(a, flops_per_launch, launch_s, dev):
+    """The arithmetic pipe that bounds this workload and the fraction of it achieved:
+    the tensor cores for the tensor-memory kernels (measured TF32 throughput divided by
+    the TF32 products per update: 4 for the LU, 3 for Parlett-Reid), the FP32 / FP64 FMA
+    pipes otherwise -- all measured live on this GPU."""
+    kern = kernel_name(a)
+    pk = pipe_peaks(dev)
+    achieved = flops_per_launch / launch_s / 1e12
+    if kern in TC_KERNEL.values():
+        products = 4 if a.op == "slogdet" else 3
+        pipe, peak = f"tcgen05 kind::tf32, {products} products per update (measured TF32 / {products})", \
+            pk["tf32"] / products
+    elif a.dtype in ("f32", "c64"):
+        pipe, peak = "fp32 FFMA (measured)", pk["ffma"]
+    else:
+        pipe, peak = "fp64 DFMA (measured)", pk["dfma"]
+    return {"pipe": pipe, "achieved_tflops": achieved, "peak_tflops": peak, "frac": achieved / peak}
+
+
+def count_launches(fn):
+    """Kernels launched by one call of fn, counted by the CUDA profiler (CUPTI); None when
+    the profiler is unavailable."""
+    import torch
+
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type.name == "CUDA" and
+                 not e.name.lower().startswith(("memcpy", "memset"))]
+        return len(names), sorted(set(names))
+    except Exception as e:  # pragma: no cover - profiler not available
+        return None, [f"profiler unavailable: {type(e).__name__}: {e}"]
+
+
+# --------------------------------------------------------------- GPU arm
+class Ctx:
+    """Per-process state of the GPU arm: device, ranks, the process group."""
+
+    def __init__(self, rank, world, local):
+        import torch
+
+        self.rank, self.world, self.local = rank, world, local
+        torch.cuda.set_device(local)
+        self.dev = torch.device("cuda", local)
+        self.dist = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=self.dev)
+            self.dist = dist
+        self.gpu_index = (local if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                          os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+
+    def barrier(self):
+        import torch
+
+        if self.dist is not None:
+            self.dist.barrier()
+        torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, x):
+        import torch
+
+        if self.dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def measure(a, ctx, cpu=True, e2e=True):
+    """One workload on this rank's GPU: the device-resident throughput of K timed steps
+    (max over ranks), the end-to-end rate through the C ABI with host buffers, the
+    rooflines, the kernel launches of one step, the clocks and (rank 0, N = 1) the CPU
+    baseline. For N > 1 every step also all-gathers the (sign, logabs) of the whole
+    sharded batch (fermix_b200.sharded.all_gather_slog, the only collective)."""
+    import torch
+
+    from fermix_b200 import _lib
+
+    dev, rank, world = ctx.dev, ctx.rank, ctx.world
     L = _lib.lib()
     tdt = {"f32": torch.float32, "f64": torch.float64, "c64": torch.complex64, "c128": torch.complex128}[a.dtype]
     rdt = torch.float32 if a.dtype in ("f32", "c64") else torch.float64
     kind = {"f32": 0, "f64": 1, "c64": 2, "c128": 3}[a.dtype]
     prec = {"tf32x3": 1, "ieee": 2}[a.prec]
+    planar = bool(a.planar) and a.dtype in ("c64", "c128")
     B, n = a.batch, a.n
     g = torch.Generator(device=dev)
     g.manual_seed(a.seed + 1000 * rank)
+    PHI = None
     if a.gather:
         if a.op != "slogdet" or a.gather < n:
             raise SystemExit("--gather needs --op slogdet and SITES >= n")
@@ -532,96 +604,83 @@ def main():
         OCC = torch.rand((B, a.gather), generator=g, device=dev).argsort(dim=1)[:, :n].sort(dim=1).values
         dup = torch.rand(B, generator=g, device=dev) < 0.02
         OCC[dup, 1] = OCC[dup, 0]
-        OCC = OCC.to(torch.int32).contiguous()
-        A = OCC  # the per-step device input
+        inputs = [OCC.to(torch.int32).contiguous()]
     else:
         A = torch.randn((B, n, n), generator=g, device=dev, dtype=tdt)
         if a.op == "slogpf":
             A = (A - A.transpose(-1, -2)).contiguous()
+        if planar:
+            inputs = [A.real.contiguous(), A.imag.contiguous()]
+            del A
+        else:
+            inputs = [A]
     sign = torch.empty(B, dtype=tdt, device=dev)
     logabs = torch.empty(B, dtype=rdt, device=dev)
-    G = None if a.fwd_only else torch.empty((B, n, n), dtype=tdt, device=dev)
+    grads = [] if a.fwd_only else ([torch.empty((B, n, n), dtype=rdt, device=dev) for _ in range(2)] if planar
+                                   else [torch.empty((B, n, n), dtype=tdt, device=dev)])
     op = _lib.FX_OP_SLOGPF if a.op == "slogpf" else _lib.FX_OP_SLOGDET
-    if a.gather:
-        wsb = L.fermix_slogdet_gather_workspace_bytes(kind, prec, B, n, 0 if a.fwd_only else 1)
-    else:
-        wsb = L.fermix_workspace_bytes(op, kind, B, n, 0 if a.fwd_only else 1)
-    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    sp = stream.cuda_stream
+    grad = 0 if a.fwd_only else 1
 
-    def call(X, Gout):
+    def ws_bytes(cnt):
         if a.gather:
-            st = L.fermix_slogdet_gather(sp, kind, prec, B, n, PHI.data_ptr(), a.gather, n, X.data_ptr(), None, 0,
-                                         sign.data_ptr(), logabs.data_ptr(), None,
-                                         None if Gout is None else Gout.data_ptr(), ws.data_ptr(), wsb)
-            _lib.check(st)
-            return
-        if a.op == "slogpf":
-            if a.fwd_only:
-                st = L.fermix_slogpf(sp, kind, prec, B, n, 1, X.data_ptr(), sign.data_ptr(), logabs.data_ptr(),
-                                     None, ws.data_ptr(), wsb)
-            else:
-                st = L.fermix_slogpf_grad(sp, kind, prec, B, n, 1, X.data_ptr(), None, 0, 0, sign.data_ptr(),
-                                          logabs.data_ptr(), None, Gout.data_ptr(), ws.data_ptr(), wsb)
+            return L.fermix_slogdet_gather_workspace_bytes(kind, prec, cnt, n, grad)
+        if planar:
+            return L.fermix_workspace_bytes_planar(op, kind, cnt, n, grad)
+        return L.fermix_workspace_bytes(op, kind, cnt, n, grad)
+
+    wsb = ws_bytes(B)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+    def call(b0, cnt, xs, gs, strm, wsp, wsz):
+        """One C-ABI call on members [b0, b0 + cnt) of the input / gradient arrays."""
+        e_in = xs[0].element_size()
+        off = b0 * n * n
+        x = [t.data_ptr() + off * e_in for t in xs]
+        gp = [t.data_ptr() + off * t.element_size() for t in gs]
+        sp = sign.data_ptr() + b0 * sign.element_size()
+        lp = logabs.data_ptr() + b0 * logabs.element_size()
+        if a.gather:
+            st = L.fermix_slogdet_gather(strm, kind, prec, cnt, n, PHI.data_ptr(), a.gather, n,
+                                         xs[0].data_ptr() + b0 * n * 4, None, 0, sp, lp, None,
+                                         gp[0] if gp else None, wsp, wsz)
+        elif planar and a.op == "slogpf":
+            st = (L.fermix_slogpf_planar(strm, kind, prec, cnt, n, 1, x[0], x[1], sp, lp, None, wsp, wsz) if not gp else
+                  L.fermix_slogpf_grad_planar(strm, kind, prec, cnt, n, 1, x[0], x[1], None, 0, 0, sp, lp, None,
+                                              gp[0], gp[1], wsp, wsz))
+        elif planar:
+            st = (L.fermix_slogdet_planar(strm, kind, prec, cnt, n, x[0], x[1], sp, lp, None, wsp, wsz) if not gp else
+                  L.fermix_slogdet_grad_planar(strm, kind, prec, cnt, n, x[0], x[1], None, 0, 0, sp, lp, None,
+                                               gp[0], gp[1], wsp, wsz))
+        elif a.op == "slogpf":
+            st = (L.fermix_slogpf(strm, kind, prec, cnt, n, 1, x[0], sp, lp, None, wsp, wsz) if not gp else
+                  L.fermix_slogpf_grad(strm, kind, prec, cnt, n, 1, x[0], None, 0, 0, sp, lp, None, gp[0], wsp, wsz))
         else:
-            if a.fwd_only:
-                st = L.fermix_slogdet(sp, kind, prec, B, n, X.data_ptr(), sign.data_ptr(), logabs.data_ptr(), None,
-                                      ws.data_ptr(), wsb)
-            else:
-                st = L.fermix_slogdet_grad(sp, kind, prec, B, n, X.data_ptr(), None, 0, 0, sign.data_ptr(),
-                                           logabs.data_ptr(), None, Gout.data_ptr(), ws.data_ptr(), wsb)
+            st = (L.fermix_slogdet(strm, kind, prec, cnt, n, x[0], sp, lp, None, wsp, wsz) if not gp else
+                  L.fermix_slogdet_grad(strm, kind, prec, cnt, n, x[0], None, 0, 0, sp, lp, None, gp[0], wsp, wsz))
         _lib.check(st)
 
-    def call_chunk(b0, cnt, X, Gout, strm):
-        """One C-ABI call on matrices [b0, b0 + cnt) of X / Gout (the e2e pipeline's
-        chunks), on stream strm."""
-        es = X.element_size()
-        off = b0 * n * n * es
-        sgn_p = sign.data_ptr() + b0 * sign.element_size()
-        la_p = logabs.data_ptr() + b0 * logabs.element_size()
-        g_p = None if Gout is None else Gout.data_ptr() + off
-        x_p = X.data_ptr() + off
-        wsc = L.fermix_workspace_bytes(op, kind, cnt, n, 0 if a.fwd_only else 1)
-        wsp = wsc_buf[strm].data_ptr() if wsc else None
-        if a.op == "slogpf":
-            if a.fwd_only:
-                st = L.fermix_slogpf(strm, kind, prec, cnt, n, 1, x_p, sgn_p, la_p, None, wsp, wsc)
-            else:
-                st = L.fermix_slogpf_grad(strm, kind, prec, cnt, n, 1, x_p, None, 0, 0, sgn_p, la_p, None, g_p, wsp,
-                                          wsc)
-        else:
-            if a.fwd_only:
-                st = L.fermix_slogdet(strm, kind, prec, cnt, n, x_p, sgn_p, la_p, None, wsp, wsc)
-            else:
-                st = L.fermix_slogdet_grad(strm, kind, prec, cnt, n, x_p, None, 0, 0, sgn_p, la_p, None, g_p, wsp,
-                                           wsc)
-        _lib.check(st)
+    stream = torch.cuda.current_stream(dev)
+    gather_out = None
+    if world > 1:
+        from fermix_b200 import sharded
 
-    wsc_buf = {}
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(x):
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        def step():
+            call(0, B, inputs, grads, stream.cuda_stream, ws.data_ptr(), wsb)
+            # the sharded batch's (sign, logabs) on every rank: the only collective
+            nonlocal gather_out
+            gather_out = sharded.all_gather_slog(sign, logabs, B * world)
+    else:
+        def step():
+            call(0, B, inputs, grads, stream.cuda_stream, ws.data_ptr(), wsb)
 
     # ---- device-resident timing
     for _ in range(a.warmup):
-        call(A, G)
-    barrier()
-    clocks = Clocks(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
-                    os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+        step()
+    ctx.barrier()
+    clocks = Clocks(ctx.gpu_index)
     clocks.start()
     time.sleep(0.2)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
+    ctx.barrier()
     if a.gather:
         # the gathered inputs fit in L2: flush it (write 256 MB) before every step and time
         # each step's launch alone
@@ -630,25 +689,28 @@ def main():
         for f0, f1 in evs:
             flush.fill_(1)
             f0.record(stream)
-            call(A, G)
+            step()
             f1.record(stream)
-        barrier()
+        ctx.barrier()
         t_dev = sum(f0.elapsed_time(f1) for f0, f1 in evs) / 1e3
+        del flush
     else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(a.steps):
-            call(A, G)
+            step()
         e1.record(stream)
-        barrier()
+        ctx.barrier()
         t_dev = e0.elapsed_time(e1) / 1e3
     ck = clocks.stop()
-    t_dev = max_over_ranks(t_dev)
+    t_dev = ctx.max_over_ranks(t_dev)
     value = world * B * a.steps / t_dev
-    ms_step = 1e3 * t_dev / a.steps
     fl, by = flops_bytes(a)
-    launch_s = t_dev / a.steps  # one launch per step
+    launch_s = t_dev / a.steps
     hbm, peak_kind = peaks()
     achieved = B * by / launch_s / 1e9
+    cr = compute_roofline(a, B * fl, launch_s, dev)
+    t_hbm, t_pipe = B * by / (hbm * 1e9), B * fl / (cr["peak_tflops"] * 1e12)
     roofline = {
         "bound": "hbm",
         "achieved": achieved,
@@ -661,129 +723,215 @@ def main():
         "algorithmic_bytes_per_launch": B * by,
         "flops_per_launch": B * fl,
         "achieved_tflops": B * fl / launch_s / 1e12,
+        "binding": "hbm" if t_hbm >= t_pipe else cr["pipe"],
+        "binding_frac": max(t_hbm, t_pipe) / launch_s,
     }
+    launches, kernels = count_launches(step)
 
     # ---- end to end through the C ABI with host buffers
-    e2e = None
-    if not a.no_e2e:
-        hA = torch.empty(A.shape, dtype=A.dtype, pin_memory=True)
-        hA.copy_(A)
-        dA = torch.empty_like(A)
+    e2e_line = None
+    if e2e:
+        hin = []
+        for t in inputs:
+            h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            h.copy_(t)
+            hin.append(h)
+        din = [torch.empty_like(t) for t in inputs]
         hS = torch.empty(B, dtype=tdt, pin_memory=True)
         hL = torch.empty(B, dtype=rdt, pin_memory=True)
-        hG = None if a.fwd_only else torch.empty((B, n, n), dtype=tdt, pin_memory=True)
-        dG = None if a.fwd_only else torch.empty((B, n, n), dtype=tdt, device=dev)
+        hG = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in grads]
         hP = None
-        if a.gather:
+        if PHI is not None:
             hP = torch.empty(PHI.shape, dtype=tdt, pin_memory=True)
             hP.copy_(PHI)
         ke = max(3, min(a.steps, 20))
         # the step in CH chunks on three streams (copy in, compute, copy out), so that the
         # two copy directions and the compute overlap; every call goes through the C ABI
-        CH = 1 if a.gather else 8
+        CH = 1 if a.gather else min(8, B)
         s_in, s_cmp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
         bounds = [(B * c // CH, B * (c + 1) // CH) for c in range(CH)]
-        if not a.gather:
-            wmax = L.fermix_workspace_bytes(op, kind, max(e - b for b, e in bounds), n, 0 if a.fwd_only else 1)
-            wsc_buf[s_cmp.cuda_stream] = torch.empty(max(wmax, 1), dtype=torch.uint8, device=dev)
+        wmax = ws_bytes(max(e - b for b, e in bounds))
+        wsc = torch.empty(max(wmax, 1), dtype=torch.uint8, device=dev)
 
         def e2e_step():
-            if a.gather:
-                if hP is not None:
-                    PHI.copy_(hP, non_blocking=True)
-                dA.copy_(hA, non_blocking=True)
-                call(dA, dG)
-                hS.copy_(sign, non_blocking=True)
-                hL.copy_(logabs, non_blocking=True)
-                if hG is not None:
-                    hG.copy_(dG, non_blocking=True)
-                return
             start = torch.cuda.Event()
             start.record(stream)
             for s_ in (s_in, s_cmp, s_out):
                 s_.wait_event(start)
+            if hP is not None:
+                with torch.cuda.stream(s_in):
+                    PHI.copy_(hP, non_blocking=True)
             for b0, b1 in bounds:
                 with torch.cuda.stream(s_in):
-                    dA[b0:b1].copy_(hA[b0:b1], non_blocking=True)
+                    for d, h in zip(din, hin):
+                        d[b0:b1].copy_(h[b0:b1], non_blocking=True)
                 ev_in = torch.cuda.Event()
                 ev_in.record(s_in)
                 s_cmp.wait_event(ev_in)
-                call_chunk(b0, b1 - b0, dA, dG, s_cmp.cuda_stream)
+                call(b0, b1 - b0, din, grads, s_cmp.cuda_stream, wsc.data_ptr(), wmax)
                 ev_c = torch.cuda.Event()
                 ev_c.record(s_cmp)
                 s_out.wait_event(ev_c)
                 with torch.cuda.stream(s_out):
                     hS[b0:b1].copy_(sign[b0:b1], non_blocking=True)
                     hL[b0:b1].copy_(logabs[b0:b1], non_blocking=True)
-                    if hG is not None:
-                        hG[b0:b1].copy_(dG[b0:b1], non_blocking=True)
+                    for h, d in zip(hG, grads):
+                        h[b0:b1].copy_(d[b0:b1], non_blocking=True)
             done = torch.cuda.Event()
             done.record(s_out)
             stream.wait_event(done)
 
         for _ in range(2):
             e2e_step()
-        barrier()
+        ctx.barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
         for _ in range(ke):
             e2e_step()
         f1.record(stream)
-        barrier()
-        t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
-        h2d = A.numel() * A.element_size() + (0 if hP is None else hP.numel() * hP.element_size())
-        d2h = sign.numel() * sign.element_size() + logabs.numel() * logabs.element_size()
-        if hG is not None:
-            d2h += hG.numel() * hG.element_size()
-        e2e = {"value": world * B * ke / t_e2e, "unit": "matrices/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "steps": ke}
+        ctx.barrier()
+        t_e2e = ctx.max_over_ranks(f0.elapsed_time(f1) / 1e3)
+        h2d = sum(h.numel() * h.element_size() for h in hin) + (0 if hP is None else hP.numel() * hP.element_size())
+        d2h = hS.numel() * hS.element_size() + hL.numel() * hL.element_size()
+        d2h += sum(h.numel() * h.element_size() for h in hG)
+        e2e_line = {"value": world * B * ke / t_e2e, "unit": "matrices/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": ke}
+        del hin, din, hG, wsc
 
-    cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu:
+    cpu_line = None
+    if cpu and rank == 0 and world == 1 and a.cpu_sample > 0:
         threads = os.cpu_count() or 1
-        r, dt = cpu_rate(a, a.cpu_sample, threads)
-        cpu = {"value": r, "unit": "matrices/s", "cores": threads, "kind": "port",
-               "sample": f"{a.cpu_sample} matrices of the same workload ({dt:.1f} s; numpy/LAPACK restatement of "
-                         "the reference's generic path, all host threads)"}
+        ca = argparse.Namespace(**vars(a))
+        if a.cpu_n:
+            ca.n = a.cpu_n
+        r, dt = cpu_rate(ca, a.cpu_sample, threads)
+        note = ""
+        if a.cpu_n and a.cpu_n != a.n:
+            note = (f"; timed at n = {a.cpu_n} because the restatement takes minutes per matrix at n = {a.n}: "
+                    f"value is the n = {a.cpu_n} rate, est_value_at_n scales it by (n_sample / n)^3")
+        cpu_line = {"value": r, "unit": "matrices/s", "cores": threads, "kind": "port",
+                    "sample": f"{a.cpu_sample} matrices of the same workload ({dt:.1f} s; numpy/LAPACK restatement of "
+                              f"the reference's generic path, all host threads){note}"}
+        if note:
+            cpu_line["n_sample"] = a.cpu_n
+            cpu_line["est_value_at_n"] = r * (a.cpu_n / a.n) ** 3
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "matrices/s",
+        "n_gpus": world,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": 1e3 * t_dev / a.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": a.dtype,
+        "data": ("synthetic (seeded iid N(0,1), S = A - A^T)" if a.op == "slogpf" else
+                 "synthetic (seeded phi ~ N(0, 1/sqrt(n)), random sorted occupations, 2% duplicated rows)"
+                 if a.gather else "synthetic (seeded iid N(0,1))") + (", split re/im planes" if planar else ""),
+        "config": {
+            "workload": workload_name(a),
+            "op": a.op,
+            "pass": "fwd" if a.fwd_only else "fwd+bwd",
+            "batch_per_gpu": B,
+            "n": n,
+            "prec": a.prec,
+            "layout": "planar (split re/im)" if planar else "interleaved",
+            "parallelism": (f"batch sharded x{world}; (sign, logabs) all-gathered every step" if world > 1
+                            else "one GPU"),
+            "l2": ("L2 flushed before every timed step" if a.gather else
+                   "inputs exceed L2 (no flush needed)" if B * n * n * inputs[0].element_size() * len(inputs) > 126e6
+                   else "inputs fit L2"),
+        },
+        "roofline": roofline,
+        "compute_roofline": cr,
+        "cpu_baseline": cpu_line,
+        "e2e": e2e_line,
+        "gpu_launches": None if launches is None else launches * a.steps,
+        "gpu_launches_per_step": launches,
+        "kernels": kernels,
+        "clocks": ck,
+    }
+    del inputs, grads, ws
+    torch.cuda.empty_cache()
+    return line
 
+
+# the default run's per-configuration entries (C5 on bounded batch
+# samples). Keys override the headline arguments.
+PER_CONFIG = [
+    ("C1 slogdet fwd", dict(op="slogdet", fwd_only=True)),
+    ("C2 slogpf fwd tf32x3", dict(fwd_only=True, cpu_sample=128)),
+    ("C2 slogpf fwd+bwd tf32x3", dict()),
+    ("C2 slogpf fwd ieee", dict(fwd_only=True, prec="ieee", steps=10, cpu_sample=128)),
+    ("C2 slogpf fwd+bwd ieee", dict(prec="ieee", steps=10, cpu_sample=128)),
+    ("C3 slogdet fwd (materialised)", dict(op="slogdet", n=256, batch=16384, fwd_only=True, steps=10, cpu_sample=256)),
+    ("C3 slogdet fwd+bwd (materialised)", dict(op="slogdet", n=256, batch=16384, steps=10, cpu_sample=128)),
+    ("C3 slogdet fwd (gathered from phi)", dict(op="slogdet", n=256, batch=16384, gather=512, fwd_only=True, steps=10,
+                                                cpu_sample=256)),
+    ("C3 slogdet fwd+bwd (gathered from phi)", dict(op="slogdet", n=256, batch=16384, gather=512, steps=10,
+                                                    cpu_sample=128)),
+    ("C4 slogpf fwd c64 planar", dict(dtype="c64", n=512, batch=2048, fwd_only=True, planar=True, steps=5, warmup=3,
+                                      cpu_sample=2, cpu_n=256)),
+    ("C4 slogpf fwd+bwd c64 planar", dict(dtype="c64", n=512, batch=2048, planar=True, steps=5, warmup=3, cpu_sample=2,
+                                          cpu_n=256)),
+    ("C5a slogdet fwd f64 n4096 (B=16 sample)", dict(op="slogdet", dtype="f64", prec="ieee", n=4096, batch=16,
+                                                     fwd_only=True, steps=3, warmup=3, cpu_sample=2)),
+    ("C5a slogdet fwd+bwd f64 n4096 (B=16 sample)", dict(op="slogdet", dtype="f64", prec="ieee", n=4096, batch=16,
+                                                         steps=3, warmup=3, cpu_sample=1)),
+    ("C5b slogpf fwd c128 n4096 (B=4 sample)", dict(dtype="c128", prec="ieee", n=4096, batch=4, fwd_only=True, steps=3,
+                                                    warmup=3, cpu_sample=1, cpu_n=512)),
+    ("C5b slogpf fwd+bwd c128 n4096 (B=4 sample)", dict(dtype="c128", prec="ieee", n=4096, batch=4, steps=3, warmup=3,
+                                                        cpu_sample=1, cpu_n=512)),
+]
+
+SLIM = ("value", "ms_per_step", "roofline", "compute_roofline", "cpu_baseline", "e2e", "gpu_launches_per_step",
+        "clocks")
+
+
+def per_config(a, ctx, headline):
+    out = []
+    for name, over in PER_CONFIG:
+        if not over:
+            line = headline
+        else:
+            b = argparse.Namespace(**vars(a))
+            b.steps, b.warmup, b.cpu_sample = min(a.steps, 20), max(a.warmup, 3), 512
+            for k, v in over.items():
+                setattr(b, k, v)
+            line = measure(b, ctx)
+        entry = {"config": name, "workload": line["config"]["workload"], "pass": line["config"]["pass"],
+                 "layout": line["config"]["layout"], "dtype": line["dtype"], "steps": line["steps"]}
+        entry.update({k: line[k] for k in SLIM})
+        if entry["roofline"]:
+            entry["roofline"] = {k: entry["roofline"][k] for k in ("achieved", "peak", "frac", "kernel", "binding",
+                                                                   "binding_frac", "achieved_tflops")}
+        out.append(entry)
+        if ctx.rank == 0:
+            print(f"# {name}: {line['value']:.1f} mat/s", file=sys.stderr, flush=True)
+    return out
+
+
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank)
+        return
+    if a.move:
+        run_move(a, rank, world, local)
+        return
+    ctx = Ctx(rank, world, local)
+    line = measure(a, ctx, cpu=not a.no_cpu, e2e=not a.no_e2e)
+    pc = a.per_config == "on" or (a.per_config == "auto" and world == 1 and a.is_default)
+    if pc:
+        line["per_config"] = per_config(a, ctx, line)
     if rank == 0:
-        line = {
-            "metric": METRIC,
-            "value": value,
-            "unit": "matrices/s",
-            "n_gpus": world,
-            "steps": a.steps,
-            "warmup": a.warmup,
-            "ms_per_step": ms_step,
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": a.dtype,
-            "data": ("synthetic (seeded iid N(0,1), S = A - A^T)" if a.op == "slogpf" else
-                     "synthetic (seeded phi ~ N(0, 1/sqrt(n)), random sorted occupations, 2% duplicated rows)"
-                     if a.gather else "synthetic (seeded iid N(0,1))"),
-            "config": {
-                "workload": workload_name(a),
-                "op": a.op,
-                "pass": "fwd" if a.fwd_only else "fwd+bwd",
-                "batch_per_gpu": B,
-                "n": n,
-                "prec": a.prec,
-                "parallelism": f"batch sharded x{world}, no collective",
-                "l2": ("L2 flushed before every timed step" if a.gather else
-                       "inputs exceed L2 (no flush needed)" if B * n * n * A.element_size() > 126e6 else "inputs fit L2"),
-            },
-            "roofline": roofline,
-            "compute_roofline": compute_roofline(a, B * fl, launch_s),
-            "cpu_baseline": cpu,
-            "e2e": e2e,
-            "gpu_launches": a.steps * launches_per_call(a),
-            "clocks": ck,
-        }
         print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    ctx.close()
 
 
 if __name__ == "__main__":

@@ -19,8 +19,12 @@ from .api import (
     slogpf_ratio,
     slogpf_update,
     slogdet_parts,
+    slogdet_planar,
     slogpf,
     slogpf_parts,
+    slogpf_planar,
+    det_planar,
+    pf_planar,
 )
 
 __version__ = "0.1.0"
@@ -38,6 +42,10 @@ __all__ = [
     "slogdet_update",
     "slogpf_ratio",
     "slogpf_update",
+    "slogdet_planar",
+    "slogpf_planar",
+    "det_planar",
+    "pf_planar",
     "FermixFallbackWarning",
     "__version__",
 ]

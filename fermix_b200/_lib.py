@@ -40,8 +40,16 @@ SIGNATURES = {
     "fermix_strerror": (ctypes.c_char_p, [_i]),
     "fermix_version": (_i, []),
     "fermix_selftest_umma": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp]),
+    "fermix_selftest_fma_rate": (_i, [_vp, _i, _i, _i, _vp]),
     "fermix_device_status": (_i, [_i]),
     "fermix_set_wait_polls": (ctypes.c_uint, [ctypes.c_uint]),
+    "fermix_slogdet_planar": (_i, [_vp, _i, _i, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _sz]),
+    "fermix_slogdet_grad_planar": (
+        _i, [_vp, _i, _i, _i64, _i64, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _sz]),
+    "fermix_slogpf_planar": (_i, [_vp, _i, _i, _i64, _i64, _i, _vp, _vp, _vp, _vp, _vp, _vp, _sz]),
+    "fermix_slogpf_grad_planar": (
+        _i, [_vp, _i, _i, _i64, _i64, _i, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _sz]),
+    "fermix_workspace_bytes_planar": (_sz, [_i, _i, _i64, _i64, _i]),
     # include/fermix_b200_xla.h
     "fermix_xla_custom_call": (None, [_vp, _vp, ctypes.c_char_p, _sz]),
     "fermix_xla_last_error": (_i, [_i]),

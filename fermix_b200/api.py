@@ -672,3 +672,77 @@ def pf_parts(a, *, prec=None, skew_symmetrize=True, coef=None):
     """(pf, G) from one launch, G = coef * pf(S) S^-T / 2 (the reference's jax.grad of
     sum(Re pf))."""
     return _parts(_lib.FX_OP_SLOGPF, a, prec, skew_symmetrize, True, coef)
+
+
+# ------------------------------------------------------------------ split planes
+def _planar(op, a_re, a_im, prec, skew, grad, adjugate, coef):
+    a_re, a_im = _prep(a_re), _prep(a_im)
+    if a_re.dtype not in (torch.float32, torch.float64) or a_im.dtype != a_re.dtype:
+        raise TypeError("a_re and a_im must both be float32 (complex64) or both float64 (complex128)")
+    if a_re.shape != a_im.shape or a_re.device != a_im.device:
+        raise ValueError("a_re and a_im must have the same shape and device")
+    cdt = torch.complex64 if a_re.dtype == torch.float32 else torch.complex128
+    p = _check_prec(cdt, prec)
+    re, batch, n = _flat(a_re)
+    im, _, _ = _flat(a_im)
+    B, dev, kind = re.shape[0], re.device, _KIND[cdt]
+    L = _lib.lib()
+    sign = torch.empty(B, dtype=cdt, device=dev)
+    logabs = torch.empty(B, dtype=a_re.dtype, device=dev)
+    val = torch.empty(B, dtype=cdt, device=dev) if adjugate else None
+    g_re = torch.empty_like(re) if grad else None
+    g_im = torch.empty_like(im) if grad else None
+    if coef is not None:
+        coef = torch.as_tensor(coef, device=dev).to(cdt).reshape(-1).contiguous()
+    with torch.cuda.device(dev):
+        nb = L.fermix_workspace_bytes_planar(op, kind, B, n, int(grad))
+        ws = torch.empty(nb, dtype=torch.uint8, device=dev) if nb else None
+        s = _stream_ptr(dev)
+        if op == _lib.FX_OP_SLOGDET:
+            st = (L.fermix_slogdet_grad_planar(s, kind, p, B, n, _ptr(re), _ptr(im), _ptr(coef), 0, int(adjugate),
+                                               _ptr(sign), _ptr(logabs), _ptr(val), _ptr(g_re), _ptr(g_im), _ptr(ws), nb)
+                  if grad else
+                  L.fermix_slogdet_planar(s, kind, p, B, n, _ptr(re), _ptr(im), _ptr(sign), _ptr(logabs), _ptr(val),
+                                          _ptr(ws), nb))
+        else:
+            st = (L.fermix_slogpf_grad_planar(s, kind, p, B, n, int(skew), _ptr(re), _ptr(im), _ptr(coef), 0,
+                                              int(adjugate), _ptr(sign), _ptr(logabs), _ptr(val), _ptr(g_re),
+                                              _ptr(g_im), _ptr(ws), nb)
+                  if grad else
+                  L.fermix_slogpf_planar(s, kind, p, B, n, int(skew), _ptr(re), _ptr(im), _ptr(sign), _ptr(logabs),
+                                         _ptr(val), _ptr(ws), nb))
+    _lib.check(st)
+    shape = batch + (n, n)
+    out = (sign.reshape(batch), logabs.reshape(batch))
+    if adjugate:
+        out = (val.reshape(batch),)
+    if grad:
+        out = out + (g_re.reshape(shape), g_im.reshape(shape))
+    return out
+
+
+def slogdet_planar(a_re, a_im, *, prec=None, grad=False, coef=None):
+    """slogdet of complex matrices given as split real and imaginary planes a_re, a_im
+    (float32 for complex64, float64 for complex128; shape (..., n, n)). Returns (sign,
+    logabs), plus (g_re, g_im) -- the planes of coef * A^-T, the reference's jax.grad of
+    sum(logabs) -- when grad. Equal bit for bit to slogdet / slogdet_parts on a_re + i a_im;
+    for n > 256 the kernels read and write the planes directly. Not differentiable."""
+    return _planar(_lib.FX_OP_SLOGDET, a_re, a_im, prec, True, grad, False, coef)
+
+
+def slogpf_planar(a_re, a_im, *, prec=None, skew_symmetrize=True, grad=False, coef=None):
+    """slogpf of complex skew matrices given as split real and imaginary planes (see
+    slogdet_planar); the gradient planes are those of coef * S^-T / 2."""
+    return _planar(_lib.FX_OP_SLOGPF, a_re, a_im, prec, skew_symmetrize, grad, False, coef)
+
+
+def det_planar(a_re, a_im, *, prec=None, grad=False, coef=None):
+    """det of complex matrices given as split planes: (det,) plus the planes of
+    coef * adj(A)^T when grad."""
+    return _planar(_lib.FX_OP_SLOGDET, a_re, a_im, prec, True, grad, True, coef)
+
+
+def pf_planar(a_re, a_im, *, prec=None, skew_symmetrize=True, grad=False, coef=None):
+    """pf of complex skew matrices given as split planes: (pf,) plus the planes of
+    coef * pf(S) S^-T / 2 when grad."""
+    return _planar(_lib.FX_OP_SLOGPF, a_re, a_im, prec, skew_symmetrize, grad, True, coef)

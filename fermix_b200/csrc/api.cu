@@ -84,10 +84,32 @@ int launch_poly(cudaStream_t s, const Job<T>& J, int is_pf) {
   return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
 }
 
+// Split real / imaginary planes of a complex call's input and gradient (the blocked
+// engines read and write them directly).
+template <typename T>
+struct Planes {
+  typedef typename Sc<T>::R R;
+  const R* a_re;
+  const R* a_im;
+  R* g_re;
+  R* g_im;
+};
+
+template <typename T>
+void set_planes(Job<T>& J, const Planes<T>* pl) {
+  if (!pl) return;
+  J.a_re = pl->a_re;
+  J.a_im = pl->a_im;
+  J.g_re = pl->g_re;
+  J.g_im = pl->g_im;
+}
+
 template <typename T>
 int run_det(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* a, const void* coef, int conj_out,
-            int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb) {
+            int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb,
+            const Planes<T>* pl = nullptr) {
   Job<T> J = make_job<T>(batch, n, a, coef, conj_out, 0, mode, sign, logabs, value, grad);
+  set_planes(J, pl);
   if (n <= DET_POLY_MAX) return launch_poly<T>(s, J, 0);
   if constexpr (std::is_same<T, float>::value) {
     if (use_lu_tc(1, prec, (int)n, mode)) return launch_lu_tc(s, J);
@@ -118,8 +140,10 @@ int run_det(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* a, c
 
 template <typename T>
 int run_pf(cudaStream_t s, int prec, int64_t batch, int64_t n, int skew, const void* a, const void* coef, int conj_out,
-           int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb) {
+           int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb,
+           const Planes<T>* pl = nullptr) {
   Job<T> J = make_job<T>(batch, n, a, coef, conj_out, skew, mode, sign, logabs, value, grad);
+  set_planes(J, pl);
   if (n % 2 == 1) {
     if (grad && batch * n * n > 0 &&
         cudaMemsetAsync(grad, 0, (size_t)batch * n * n * sizeof(T), s) != cudaSuccess)
@@ -201,6 +225,115 @@ size_t ws_bytes_t(int op, int64_t batch, int64_t n, int grad) {
     return m > fwd ? m : fwd;
   }
   return generic;
+}
+
+// ---------------------------------------------------------------- split planes
+// Complex calls whose input and gradient are split real / imaginary planes (the layout of
+// the reference's Field.split / join, src/fermix/_field.py:246-256). The blocked engines
+// (n > 256: slogdet / slogpf forward and slog gradient) read and write the planes in their
+// copy-in and gradient kernels, so the planar call moves the same bytes as the interleaved
+// one. Every other case goes through the workspace in chunks: the chunk is interleaved,
+// the interleaved path runs on it, and its gradient is split back into planes.
+template <typename T>
+__global__ void __launch_bounds__(256) interleave_kernel(T* out, const typename Sc<T>::R* re,
+                                                         const typename Sc<T>::R* im, size_t count) {
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < count; e += (size_t)gridDim.x * blockDim.x)
+    out[e] = T{re[e], im[e]};
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) split_kernel(typename Sc<T>::R* re, typename Sc<T>::R* im, const T* in,
+                                                    size_t count) {
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < count; e += (size_t)gridDim.x * blockDim.x) {
+    const T v = in[e];
+    re[e] = v.re;
+    im[e] = v.im;
+  }
+}
+
+inline unsigned elementwise_grid(size_t count) {
+  const size_t blocks = (count + 255) / 256;
+  return (unsigned)(blocks < 148 * 16 ? blocks : 148 * 16);
+}
+
+bool planar_native(bool pf, int64_t n, int mode) {
+  if (n <= kSmallMax || (mode != MODE_FWD && mode != MODE_SLOG_GRAD)) return false;
+  return !pf || (n % 2 == 0 && n <= kPflMaxN);
+}
+
+// matrices per chunk of the converting route: the whole batch up to about 1 GiB per plane copy
+template <typename T>
+int64_t planar_chunk(int64_t batch, int64_t n) {
+  const size_t per = (size_t)n * n * sizeof(T);
+  int64_t c = per ? (int64_t)(((size_t)1 << 30) / per) : batch;
+  if (c < 1) c = 1;
+  return batch < c ? batch : c;
+}
+
+template <typename T>
+size_t planar_ws_bytes(int op, int64_t batch, int64_t n, int grad) {
+  const int mode = grad ? MODE_SLOG_GRAD : MODE_FWD;
+  if (planar_native(op == FX_OP_SLOGPF, n, mode)) return ws_bytes_t<T>(op, batch, n, grad);
+  const int64_t c = planar_chunk<T>(batch, n);
+  const size_t m = align256((size_t)c * n * n * sizeof(T));
+  return m * (grad ? 2 : 1) + ws_bytes_t<T>(op, c, n, grad);
+}
+
+template <typename T>
+int run_planar(cudaStream_t s, bool pf, int prec, int64_t batch, int64_t n, int skew, const void* re, const void* im,
+               const void* coef, int conj_out, int mode, void* sign, void* logabs, void* value, void* g_re,
+               void* g_im, void* ws, size_t wsb) {
+  typedef typename Sc<T>::R R;
+  Planes<T> pl{static_cast<const R*>(re), static_cast<const R*>(im), static_cast<R*>(g_re), static_cast<R*>(g_im)};
+  if (planar_native(pf, n, mode)) {
+    return pf ? run_pf<T>(s, prec, batch, n, skew, nullptr, coef, conj_out, mode, sign, logabs, value, nullptr, ws, wsb,
+                          &pl)
+              : run_det<T>(s, prec, batch, n, nullptr, coef, conj_out, mode, sign, logabs, value, nullptr, ws, wsb,
+                           &pl);
+  }
+  const bool grad = mode != MODE_FWD;
+  const int64_t c = planar_chunk<T>(batch, n);
+  const size_t m = align256((size_t)c * n * n * sizeof(T));
+  const size_t need = m * (grad ? 2 : 1);
+  if (n > 0 && (!ws || wsb < need)) return FX_ERR_WORKSPACE;
+  unsigned char* w = static_cast<unsigned char*>(ws);
+  T* A = reinterpret_cast<T*>(w);
+  T* G = grad ? reinterpret_cast<T*>(w + m) : nullptr;
+  void* rest = n > 0 ? w + need : ws;
+  const size_t rest_b = n > 0 ? wsb - need : wsb;
+  const size_t nn = (size_t)n * n;
+  for (int64_t b0 = 0; b0 < batch; b0 += c) {
+    const int64_t cnt = batch - b0 < c ? batch - b0 : c;
+    const size_t count = (size_t)cnt * nn;
+    if (count) {
+      interleave_kernel<T><<<elementwise_grid(count), 256, 0, s>>>(A, pl.a_re + b0 * nn, pl.a_im + b0 * nn, count);
+      if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+    }
+    T* sg = static_cast<T*>(sign) + b0;
+    R* la = static_cast<R*>(logabs) + b0;
+    T* val = value ? static_cast<T*>(value) + b0 : nullptr;
+    const T* cf = coef ? static_cast<const T*>(coef) + b0 : nullptr;
+    const int e = pf ? run_pf<T>(s, prec, cnt, n, skew, A, cf, conj_out, mode, sg, la, val, G, rest, rest_b)
+                     : run_det<T>(s, prec, cnt, n, A, cf, conj_out, mode, sg, la, val, G, rest, rest_b);
+    if (e) return e;
+    if (grad && count) {
+      split_kernel<T><<<elementwise_grid(count), 256, 0, s>>>(pl.g_re + b0 * nn, pl.g_im + b0 * nn, G, count);
+      if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+    }
+  }
+  return FX_OK;
+}
+
+// complex dtypes only
+template <typename F>
+int by_complex(int dtype, F&& f) {
+  switch (dtype) {
+    case FX_C64:
+      return f(c64_t());
+    case FX_C128:
+      return f(c128_t());
+  }
+  return FX_ERR_DTYPE;
 }
 
 // ---------------------------------------------------------------- gathered slogdet
@@ -354,6 +487,88 @@ int fermix_slogdet_gather(void* stream, int dtype, int prec, int64_t batch, int6
     return run_gather<T>(s, prec, batch, n, phi, phi_rows, phi_ld, occ, coef, conj_out, sign, logabs, value, grad,
                          workspace, workspace_bytes);
   });
+}
+
+int fermix_slogdet_planar(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a_re,
+                          const void* a_im, void* sign, void* logabs, void* value, void* workspace,
+                          size_t workspace_bytes) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (dtype != FX_C64 && dtype != FX_C128) return FX_ERR_DTYPE;
+  if (batch == 0) return FX_OK;
+  if ((n > 0 && (!a_re || !a_im)) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_complex(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_planar<T>(s, false, prec, batch, n, 0, a_re, a_im, nullptr, 0, MODE_FWD, sign, logabs, value, nullptr,
+                         nullptr, workspace, workspace_bytes);
+  });
+}
+
+int fermix_slogdet_grad_planar(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a_re,
+                               const void* a_im, const void* coef, int conj_out, int adjugate, void* sign,
+                               void* logabs, void* value, void* grad_re, void* grad_im, void* workspace,
+                               size_t workspace_bytes) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (dtype != FX_C64 && dtype != FX_C128) return FX_ERR_DTYPE;
+  if (batch == 0) return FX_OK;
+  if ((n > 0 && (!a_re || !a_im || !grad_re || !grad_im)) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
+  return by_complex(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_planar<T>(s, false, prec, batch, n, 0, a_re, a_im, coef, conj_out, mode, sign, logabs, value, grad_re,
+                         grad_im, workspace, workspace_bytes);
+  });
+}
+
+int fermix_slogpf_planar(void* stream, int dtype, int prec, int64_t batch, int64_t n, int skew_symmetrize,
+                         const void* a_re, const void* a_im, void* sign, void* logabs, void* value, void* workspace,
+                         size_t workspace_bytes) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (dtype != FX_C64 && dtype != FX_C128) return FX_ERR_DTYPE;
+  if (batch == 0) return FX_OK;
+  if ((n > 0 && (!a_re || !a_im)) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_complex(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_planar<T>(s, true, prec, batch, n, skew_symmetrize, a_re, a_im, nullptr, 0, MODE_FWD, sign, logabs,
+                         value, nullptr, nullptr, workspace, workspace_bytes);
+  });
+}
+
+int fermix_slogpf_grad_planar(void* stream, int dtype, int prec, int64_t batch, int64_t n, int skew_symmetrize,
+                              const void* a_re, const void* a_im, const void* coef, int conj_out, int adjugate,
+                              void* sign, void* logabs, void* value, void* grad_re, void* grad_im, void* workspace,
+                              size_t workspace_bytes) {
+  int e = validate(dtype, prec, batch, n);
+  if (e) return e;
+  if (dtype != FX_C64 && dtype != FX_C128) return FX_ERR_DTYPE;
+  if (batch == 0) return FX_OK;
+  if ((n > 0 && (!a_re || !a_im || !grad_re || !grad_im)) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int mode = adjugate ? MODE_VALUE_GRAD : MODE_SLOG_GRAD;
+  return by_complex(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_planar<T>(s, true, prec, batch, n, skew_symmetrize, a_re, a_im, coef, conj_out, mode, sign, logabs,
+                         value, grad_re, grad_im, workspace, workspace_bytes);
+  });
+}
+
+size_t fermix_workspace_bytes_planar(int op, int dtype, int64_t batch, int64_t n, int grad) {
+  if (validate(dtype, FX_PREC_DEFAULT, batch, n) || batch == 0) return 0;
+  if (dtype != FX_C64 && dtype != FX_C128) return 0;
+  const size_t units = (size_t)by_complex(dtype, [&](auto t) -> int {
+    using T = decltype(t);
+    return (int)((planar_ws_bytes<T>(op, batch, n, grad) + 255) / 256);
+  });
+  return with_slack(units * 256);
 }
 
 size_t fermix_slogdet_gather_workspace_bytes(int dtype, int prec, int64_t batch, int64_t n, int grad) {

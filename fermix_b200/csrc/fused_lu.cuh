@@ -47,6 +47,13 @@ struct Job {
   int in_smem;                 // work buffers in dynamic shared memory
   T* ws;                       // global work slots (gridDim.x * nbuf * n * ld) otherwise
   uint32_t wait_polls;         // polls of each bounded wait (tensor-memory kernels)
+  // complex input / gradient as split real and imaginary planes (B, n, n) each: when a_re
+  // is set it replaces a, and when g_re is set it replaces g (read and written only by the
+  // blocked engines' copy-in and gradient kernels)
+  const typename Sc<T>::R* a_re;
+  const typename Sc<T>::R* a_im;
+  typename Sc<T>::R* g_re;
+  typename Sc<T>::R* g_im;
   // row gather (tensor-memory LU only): matrix b row i = gbase[gidx[b * n + i] * gld + 0 .. n),
   // NaN for an index outside [0, grows)
   const int* gidx;

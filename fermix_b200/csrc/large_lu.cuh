@@ -60,25 +60,56 @@ struct LgArgs {
   const T* zsign;
 };
 
+// Element reader of the caller's input: interleaved values, or split real / imaginary
+// planes for complex dtypes (re set).
+template <typename T>
+struct SrcMat {
+  typedef typename Sc<T>::R R;
+  const T* a;
+  const R* re;
+  const R* im;
+  __device__ __forceinline__ T at(size_t off) const {
+    if constexpr (Sc<T>::cx) {
+      if (re) return T{re[off], im[off]};
+    }
+    return a[off];
+  }
+  __host__ __device__ SrcMat offset(size_t off) const {
+    return SrcMat{a ? a + off : nullptr, re ? re + off : nullptr, im ? im + off : nullptr};
+  }
+};
+
+template <typename T>
+__host__ __device__ inline SrcMat<T> src_of(const Job<T>& J) {
+  return SrcMat<T>{J.a, J.a_re, J.a_im};
+}
+
 // M = (a - a^T) / 2 of matrix blockIdx.z (32 x 32 tiles through shared memory)
 template <typename T>
-__global__ void __launch_bounds__(256) lg_skew_copy_kernel(T* M, const T* a, int n) {
+__global__ void __launch_bounds__(256) lg_skew_copy_kernel(T* M, SrcMat<T> a, int n) {
   __shared__ T tile[32][33];
   typedef typename Sc<T>::R R;
   const int b = blockIdx.z, i0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const T* ab = a + (size_t)b * n * n;
+  const SrcMat<T> ab = a.offset((size_t)b * n * n);
   // tile of a^T: rows j0.., columns i0..
   for (int r = ty; r < 32; r += 8) {
     const int j = j0 + r, i = i0 + tx;
-    tile[r][tx] = (j < n && i < n) ? ab[(size_t)j * n + i] : s_zero<T>();
+    tile[r][tx] = (j < n && i < n) ? ab.at((size_t)j * n + i) : s_zero<T>();
   }
   __syncthreads();
   T* Mb = M + (size_t)b * n * n;
   for (int r = ty; r < 32; r += 8) {
     const int i = i0 + r, j = j0 + tx;
-    if (i < n && j < n) Mb[(size_t)i * n + j] = scale(sub(ab[(size_t)i * n + j], tile[tx][r]), R(0.5));
+    if (i < n && j < n) Mb[(size_t)i * n + j] = scale(sub(ab.at((size_t)i * n + j), tile[tx][r]), R(0.5));
   }
+}
+
+// M = a for `count` elements from split planes (complex dtypes only)
+template <typename T>
+__global__ void __launch_bounds__(256) lg_planar_copy_kernel(T* M, SrcMat<T> a, size_t count) {
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < count; e += (size_t)gridDim.x * blockDim.x)
+    M[e] = a.at(e);
 }
 
 template <typename T>
@@ -556,12 +587,21 @@ __global__ void __launch_bounds__(256) lg_grad_kernel(LgArgs<T> A, Job<T> J, int
     tile[jj][tx] = (j < n && k < n) ? Mb[(size_t)j * n + k] : s_zero<T>();
   }
   __syncthreads();
-  T* G = J.g + (size_t)(b0 + b) * n * n;
+  const size_t gb = (size_t)(b0 + b) * n * n;
   for (int kk = ty; kk < 32; kk += 8) {
     const int k = k0 + kk, j = j0 + tx;
     if (k < n && j < n) {
       T v = zero ? s_zero<T>() : scale(mul(f, tile[tx][kk]), A.gscale);
-      G[(size_t)pm[k] * n + j] = maybe_conj(J, v);
+      v = maybe_conj(J, v);
+      const size_t o = gb + (size_t)pm[k] * n + j;
+      if constexpr (Sc<T>::cx) {
+        if (J.g_re) {  // split planes
+          J.g_re[o] = v.re;
+          J.g_im[o] = v.im;
+          continue;
+        }
+      }
+      J.g[o] = v;
     }
   }
 }

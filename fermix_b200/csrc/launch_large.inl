@@ -11,6 +11,23 @@ namespace fxh {
 // n > kSmallMax, slogdet forward and gradient: the panel loop of large_lu.cuh over slices
 // of the batch. Workspace per matrix: the matrix itself, the panel coefficients and
 // pivot-row snapshot, L11 / U11, pivots and index arrays; each array 256-byte aligned.
+// Matrices [b0, b0 + cnt) of the caller's input into the slice buffer M: a plain copy, or
+// (a - a^T) / 2 when skew; from interleaved values or from split planes (Job::a_re).
+template <typename T>
+int lg_copy_in(cudaStream_t s, T* M, const Job<T>& J, int64_t b0, int cnt, int n, bool skew) {
+  const SrcMat<T> src = src_of(J).offset((size_t)b0 * n * n);
+  const size_t count = (size_t)cnt * n * n;
+  if (skew) {
+    lg_skew_copy_kernel<T><<<dim3((n + 31) / 32, (n + 31) / 32, cnt), 256, 0, s>>>(M, src, n);
+  } else if (src.re) {
+    const size_t blocks = (count + 255) / 256;
+    lg_planar_copy_kernel<T><<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, s>>>(M, src, count);
+  } else if (cudaMemcpyAsync(M, src.a, count * sizeof(T), cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+    return FX_ERR_CUDA;
+  }
+  return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+}
+
 constexpr int kLgSliceBlocks = 4;  // a slice holds at most SMs x 4 matrices
 
 template <typename T>
@@ -84,12 +101,7 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
     return FX_ERR_CUDA;
   for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
     const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);
-    if (pf_grad && J.skew) {
-      lg_skew_copy_kernel<T><<<dim3((n + 31) / 32, (n + 31) / 32, cnt), 256, 0, s>>>(A.M, J.a + b0 * (int64_t)n * n, n);
-    } else if (cudaMemcpyAsync(A.M, J.a + b0 * (int64_t)n * n, (size_t)cnt * n * n * sizeof(T),
-                               cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
-      return FX_ERR_CUDA;
-    }
+    if (lg_copy_in<T>(s, A.M, J, b0, cnt, n, pf_grad && J.skew)) return FX_ERR_CUDA;
     for (int k0 = 0; k0 < n; k0 += NB) {
       A.k0 = k0;
       A.kw = n - k0 < NB ? n - k0 : NB;
@@ -175,12 +187,7 @@ int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
     return FX_ERR_CUDA;
   for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
     const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);
-    if (J.skew) {
-      lg_skew_copy_kernel<T><<<dim3((n + 31) / 32, (n + 31) / 32, cnt), 256, 0, s>>>(A.M, J.a + b0 * (int64_t)n * n, n);
-    } else if (cudaMemcpyAsync(A.M, J.a + b0 * (int64_t)n * n, (size_t)cnt * n * n * sizeof(T),
-                               cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
-      return FX_ERR_CUDA;
-    }
+    if (lg_copy_in<T>(s, A.M, J, b0, cnt, n, J.skew)) return FX_ERR_CUDA;
     for (int k0 = 0; k0 < n; k0 += 2 * np_max) {
       A.k0 = k0;
       A.np = (n - k0) / 2 < np_max ? (n - k0) / 2 : np_max;

@@ -91,3 +91,39 @@ extern "C" int fermix_selftest_umma(void* stream, const float* a, const float* b
   umma_selftest_kernel<<<1, 128, 0, static_cast<cudaStream_t>(stream)>>>(a, b, c, d, negate, accumulate, dis, status);
   return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
 }
+
+// FMA-pipe throughput probe: every thread runs 8 independent FMA chains of `iters` steps
+// (16 flops per step and thread), so the issue of the FP32 / FP64 FMA pipe, not latency,
+// bounds it. The chains' sum goes to out so that nothing is optimised away.
+namespace {
+
+template <typename R>
+__global__ void __launch_bounds__(256) fma_rate_kernel(int iters, R seed, R* out) {
+  R x[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) x[c] = seed + (R)(threadIdx.x + c);
+  const R m = (R)0.999999, k = (R)1e-7;
+  for (int i = 0; i < iters; ++i) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) x[c] = fma(x[c], m, k);
+  }
+  R s = 0;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) s += x[c];
+  if (s == (R)-1.2345) out[blockIdx.x] = s;  // never true for these inputs
+}
+
+}  // namespace
+
+extern "C" int fermix_selftest_fma_rate(void* stream, int dtype, int blocks, int iters, void* out) {
+  if (!out) return FX_ERR_NULL;
+  if (blocks < 1 || iters < 1) return FX_ERR_SHAPE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == FX_F32)
+    fma_rate_kernel<float><<<blocks, 256, 0, s>>>(iters, 1.0f, static_cast<float*>(out));
+  else if (dtype == FX_F64)
+    fma_rate_kernel<double><<<blocks, 256, 0, s>>>(iters, 1.0, static_cast<double*>(out));
+  else
+    return FX_ERR_DTYPE;
+  return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+}

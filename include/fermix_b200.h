@@ -91,6 +91,32 @@ int fermix_slogpf_grad(void* stream, int dtype, int prec, int64_t batch, int64_t
                        const void* a, const void* coef, int conj_out, int adjugate, void* sign, void* logabs,
                        void* value, void* grad, void* workspace, size_t workspace_bytes);
 
+/* Complex input and gradient as split real / imaginary planes (no separate reference entry:
+ * the reference computes complex values as real planes, Field.split / join,
+ * src/fermix/_field.py:246-256, and its kernels take the planes as separate operands,
+ * _pcall src/fermix/_field.py:357-389). dtype is FX_C64 or FX_C128 (else FX_ERR_DTYPE);
+ * a_re / a_im (and grad_re / grad_im) are (batch, n, n) arrays of the real type; sign and
+ * value stay interleaved complex (batch,) arrays, logabs real. Otherwise as the
+ * interleaved entry points, with the same results bit for bit. For n > 256 (slogdet, and
+ * slogpf with even n <= 8192) forward and slog gradient read and write the planes
+ * directly; other cases pass through the workspace in chunks of about 1 GiB. Workspace:
+ * fermix_workspace_bytes_planar. */
+int fermix_slogdet_planar(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a_re,
+                          const void* a_im, void* sign, void* logabs, void* value, void* workspace,
+                          size_t workspace_bytes);
+int fermix_slogdet_grad_planar(void* stream, int dtype, int prec, int64_t batch, int64_t n, const void* a_re,
+                               const void* a_im, const void* coef, int conj_out, int adjugate, void* sign,
+                               void* logabs, void* value, void* grad_re, void* grad_im, void* workspace,
+                               size_t workspace_bytes);
+int fermix_slogpf_planar(void* stream, int dtype, int prec, int64_t batch, int64_t n, int skew_symmetrize,
+                         const void* a_re, const void* a_im, void* sign, void* logabs, void* value, void* workspace,
+                         size_t workspace_bytes);
+int fermix_slogpf_grad_planar(void* stream, int dtype, int prec, int64_t batch, int64_t n, int skew_symmetrize,
+                              const void* a_re, const void* a_im, const void* coef, int conj_out, int adjugate,
+                              void* sign, void* logabs, void* value, void* grad_re, void* grad_im, void* workspace,
+                              size_t workspace_bytes);
+size_t fermix_workspace_bytes_planar(int op, int dtype, int64_t batch, int64_t n, int grad);
+
 /* slogdet of gathered matrices (no reference counterpart; the fused gather of the QMC
  * caller in the reference's README): matrix b is rows occ[b * n + i] (int32, i < n) of phi
  * (phi_rows x phi_ld row-major, same dtype), columns 0 .. n - 1, so that the batch is
@@ -206,6 +232,13 @@ const char* fermix_strerror(int code);
  * MMA completion wait timed out. */
 int fermix_selftest_umma(void* stream, const float* a, const float* b, const float* c, float* d, int negate,
                          int accumulate, const unsigned* disable_lanes, int* status);
+
+/* FMA-pipe throughput probe (no reference counterpart; it measures the FP32 / FP64 FMA
+ * peaks the benchmark's compute roofline divides by): blocks x 256 threads, each running 8
+ * independent FMA chains of iters steps, 16 * iters flops per thread. dtype FX_F32 or
+ * FX_F64; out is a device scratch word of that type (written only in a case that does not
+ * occur). Time it with events on the stream. */
+int fermix_selftest_fma_rate(void* stream, int dtype, int blocks, int iters, void* out);
 
 /* Library version, major * 10000 + minor * 100 + patch. */
 int fermix_version(void);
