@@ -512,21 +512,24 @@ def compute_roofline(a, flops_per_launch, launch_s, dev):
     return {"pipe": pipe, "achieved_tflops": achieved, "peak_tflops": peak, "frac": achieved / peak}
 
 
-def count_launches(fn):
-    """Kernels launched by one call of fn, counted by the CUDA profiler (CUPTI); None when
-    the profiler is unavailable."""
+def count_launches(fn, reps=3):
+    """Kernels launched by one call of fn: reps calls under the CUDA profiler (CUPTI),
+    divided by reps; None when the profiler is unavailable or saw nothing."""
     import torch
 
     try:
         from torch.profiler import ProfilerActivity, profile
 
         torch.cuda.synchronize()
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            fn()
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+            for _ in range(reps):
+                fn()
             torch.cuda.synchronize()
         names = [e.name for e in prof.events() if e.device_type.name == "CUDA" and
                  not e.name.lower().startswith(("memcpy", "memset"))]
-        return len(names), sorted(set(names))
+        if not names:
+            return None, ["profiler recorded no kernels"]
+        return round(len(names) / reps), sorted(set(names))
     except Exception as e:  # pragma: no cover - profiler not available
         return None, [f"profiler unavailable: {type(e).__name__}: {e}"]
 

@@ -42,13 +42,17 @@ def _rel_rows(G, R):
     return (G - R).abs().reshape(G.shape[0], -1).amax(1) / R.abs().reshape(G.shape[0], -1).amax(1)
 
 
-def _check32(err, bound, cond, what):
-    """err <= max(bound, 2 cond eps32) per member."""
-    lim = torch.maximum(bound, 2 * cond * EPS32)
-    bad = err > lim
-    used = int((err > bound).sum())
-    assert not bool(bad.any()), (what, int(bad.sum()), float((err / lim).max()), used)
-    return used
+def _check32(err, bound, A64, what):
+    """err <= max(bound, 2 cond(A) eps32) per member; cond(A) (2-norm, from the singular
+    values) is computed only for the few members above the plain bound."""
+    over = torch.nonzero(err > bound).flatten()
+    if over.numel() == 0:
+        return 0
+    cond = _cond(A64[over])
+    lim = 2 * cond * EPS32
+    bad = err[over] > lim
+    assert not bool(bad.any()), (what, int(bad.sum()), float((err[over] / lim).max()), int(over.numel()))
+    return int(over.numel())
 
 
 def _f32_batch(B, n, seed, skew=False):
@@ -65,8 +69,7 @@ def test_c1_slogdet_f32_b4096():
     A64 = x.double()
     s64, l64 = torch.linalg.slogdet(A64)
     assert torch.equal(s.double(), s64)
-    cond = _cond(A64)
-    _check32((l.double() - l64).abs(), 1e-4 * l64.abs().clamp(min=1), cond, "C1 logabs")
+    _check32((l.double() - l64).abs(), 1e-4 * l64.abs().clamp(min=1), A64, "C1 logabs")
     # the oracle (the reference's generic path restated, float32 LAPACK) on a subsample
     so, lo = oracle.slogdet(A[:256])
     assert np.array_equal(s[:256].cpu().numpy(), so)
@@ -81,14 +84,13 @@ def test_c2_slogpf_f32_b4096_fwd_vjp(prec):
     S64 = torch.from_numpy(S).cuda().double()
     _, ld64 = torch.linalg.slogdet(S64)
     lpf64 = 0.5 * ld64  # log|pf| = log|det| / 2
-    cond = _cond(S64)
-    _check32((l.detach().double() - lpf64).abs(), 1e-4 * lpf64.abs().clamp(min=1), cond, "C2 logabs")
+    _check32((l.detach().double() - lpf64).abs(), 1e-4 * lpf64.abs().clamp(min=1), S64, "C2 logabs")
     # the sign of pf from the float64 oracle (Parlett-Reid in float64) on a 512-member
     # subsample (the vectorised CPU restatement takes ~30 ms per matrix)
     so, _ = oracle.slogpf(S[:512].astype(np.float64))
     assert np.array_equal(s.detach()[:512].cpu().numpy(), so.astype(np.float32))
     R = 0.5 * torch.linalg.inv(S64).transpose(-1, -2)
-    _check32(_rel_rows(x.grad.double(), R), torch.full_like(cond, 1e-3), cond, "C2 gradient")
+    _check32(_rel_rows(x.grad.double(), R), torch.full_like(lpf64, 1e-3), S64, "C2 gradient")
 
 
 def test_c3_qmc_slogdet_f32_b16384_fwd_grad():
@@ -111,10 +113,9 @@ def test_c3_qmc_slogdet_f32_b16384_fwd_grad():
     A64 = x.detach()[reg].double()
     s64, l64 = torch.linalg.slogdet(A64)
     assert torch.equal(s.detach()[reg].double(), s64)
-    cond = _cond(A64)
-    _check32((l.detach()[reg].double() - l64).abs(), 1e-4 * l64.abs().clamp(min=1), cond, "C3 logabs")
+    _check32((l.detach()[reg].double() - l64).abs(), 1e-4 * l64.abs().clamp(min=1), A64, "C3 logabs")
     R = torch.linalg.inv(A64).transpose(-1, -2)
-    _check32(_rel_rows(x.grad[reg].double(), R), torch.full_like(cond, 1e-3), cond, "C3 gradient")
+    _check32(_rel_rows(x.grad[reg].double(), R), torch.full_like(l64, 1e-3), A64, "C3 gradient")
 
 
 def test_c4_slogpf_c64_n512_b2048_fwd_grad():
@@ -127,14 +128,13 @@ def test_c4_slogpf_c64_n512_b2048_fwd_grad():
     for b0 in range(0, B, 256):
         Sd = S[b0:b0 + 256].to(torch.complex128)
         sd, ld = torch.linalg.slogdet(Sd)
-        cond = _cond(Sd)
         lpf = 0.5 * ld
-        _check32((l[b0:b0 + 256].double() - lpf).abs(), 1e-4 * lpf.abs().clamp(min=1), cond, "C4 logabs")
+        _check32((l[b0:b0 + 256].double() - lpf).abs(), 1e-4 * lpf.abs().clamp(min=1), Sd, "C4 logabs")
         # pf^2 = det: the phase of sign^2 against the float64 determinant's
         ph = (s[b0:b0 + 256].to(torch.complex128) ** 2 - sd).abs()
-        _check32(ph, torch.full_like(cond, 1e-4), cond, "C4 sign")
+        _check32(ph / 2, torch.full_like(lpf, 1e-4), Sd, "C4 sign")  # squaring doubles the phase error
         R = 0.5 * torch.linalg.inv(Sd).transpose(-1, -2)
-        _check32(_rel_rows(G[b0:b0 + 256].to(torch.complex128), R), torch.full_like(cond, 1e-3), cond, "C4 gradient")
+        _check32(_rel_rows(G[b0:b0 + 256].to(torch.complex128), R), torch.full_like(lpf, 1e-3), Sd, "C4 gradient")
     assert bool((s.abs() - 1).abs().max() < 1e-5)
 
 
