@@ -109,6 +109,7 @@ int run_det(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* a, c
             int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb,
             const Planes<T>* pl = nullptr) {
   Job<T> J = make_job<T>(batch, n, a, coef, conj_out, 0, mode, sign, logabs, value, grad);
+  J.prec = prec;
   set_planes(J, pl);
   if (n <= DET_POLY_MAX) return launch_poly<T>(s, J, 0);
   if constexpr (std::is_same<T, float>::value) {
@@ -143,6 +144,7 @@ int run_pf(cudaStream_t s, int prec, int64_t batch, int64_t n, int skew, const v
            int mode, void* sign, void* logabs, void* value, void* grad, void* ws, size_t wsb,
            const Planes<T>* pl = nullptr) {
   Job<T> J = make_job<T>(batch, n, a, coef, conj_out, skew, mode, sign, logabs, value, grad);
+  J.prec = prec;
   set_planes(J, pl);
   if (n % 2 == 1) {
     if (grad && batch * n * n > 0 &&

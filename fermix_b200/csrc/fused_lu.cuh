@@ -43,6 +43,7 @@ struct Job {
   int64_t B;
   int n;
   int mode;
+  int prec;                    // FX_PREC_* of the call (the blocked engines' update kind)
   int ld;                      // leading dimension of the work buffers
   int in_smem;                 // work buffers in dynamic shared memory
   T* ws;                       // global work slots (gridDim.x * nbuf * n * ld) otherwise

@@ -58,6 +58,7 @@ struct LgArgs {
   int primal;
   typename Sc<T>::R gscale;
   const T* zsign;
+  uint32_t wait_polls;  // polls of the tensor-core update's bounded completion wait
 };
 
 // Element reader of the caller's input: interleaved values, or split real / imaginary

@@ -2,8 +2,11 @@
 // slices and the host-side panel loops. Included by launch_large_real.cu and
 // launch_large_complex.cu, which instantiate it for their dtypes.
 #pragma once
+#include <type_traits>
+
 #include "dispatch.cuh"
 #include "large_pf.cuh"
+#include "large_tc.cuh"
 
 namespace fxh {
 
@@ -25,6 +28,46 @@ int lg_copy_in(cudaStream_t s, T* M, const Job<T>& J, int64_t b0, int cnt, int n
   } else if (cudaMemcpyAsync(M, src.a, count * sizeof(T), cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
     return FX_ERR_CUDA;
   }
+  return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+}
+
+// The trailing update M -= C P over rows [lo, n) x columns [lo, n) (Gauss-Jordan: lo = 0)
+// of cnt matrices: the tcgen05 3xTF32 kernel for float32 / complex64 under prec tf32x3
+// (the default of those dtypes), the DMMA kernel for complex128, and the FMA-tiled kernel
+// for float64 and for float32 / complex64 under prec ieee.
+template <typename T, bool SKEW>
+int lg_update(cudaStream_t s, const LgArgs<T>& A, int lo, int cnt, int prec) {
+  const int n = A.n;
+  if (lo >= n) return FX_OK;
+  if constexpr (std::is_same<T, float>::value || std::is_same<T, c64_t>::value) {
+    if (prec != FX_PREC_IEEE) {
+      const size_t smem = lg_tc_smem<T>();
+      void* k = (void*)&lg_tc_update_kernel<T, SKEW>;
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return FX_ERR_CUDA;
+      LgArgs<T> arg = A;
+      int r_lo = lo, c_lo = lo;
+      void* args[] = {&arg, &r_lo, &c_lo};
+      const dim3 grid((unsigned)((n - lo + 127) / 128), (unsigned)cnt);
+      return cudaLaunchKernel(k, grid, dim3(128), args, smem, s) == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+    }
+  }
+  if constexpr (std::is_same<T, c128_t>::value) {
+    // complex128: fp64 tensor cores (DMMA), IEEE fp64 FMA arithmetic. (float64 keeps the
+    // DFMA tile kernel below: on B200 the fp64 tensor and vector peaks are equal, and that
+    // kernel measured faster for the real LU update, 164 vs 134 matrices/s on C5a.)
+    constexpr int TC = LgDm<T>::TC;
+    const size_t smem = lg_dm_smem<T>();
+    void* k = (void*)&lg_dmma_update_kernel<T, SKEW>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return FX_ERR_CUDA;
+    LgArgs<T> arg = A;
+    int r_lo = lo, c_lo = lo;
+    void* args[] = {&arg, &r_lo, &c_lo};
+    const dim3 grid((unsigned)((n - lo + TC - 1) / TC), (unsigned)((n - lo + 127) / 128), (unsigned)cnt);
+    return cudaLaunchKernel(k, grid, dim3(256), args, smem, s) == cudaSuccess ? FX_OK : FX_ERR_CUDA;
+  }
+  lg_update_kernel<T, SKEW><<<dim3((n - lo + 63) / 64, (n - lo + 63) / 64, cnt), 256, 0, s>>>(A, lo, lo);
   return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
 }
 
@@ -93,6 +136,7 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
   A.primal = pf_grad ? 0 : 1;
   A.gscale = pf_grad ? typename Sc<T>::R(0.5) : typename Sc<T>::R(1);
   A.zsign = pf_grad ? J.sign : nullptr;
+  A.wait_polls = J.wait_polls;
   const size_t leaf_smem = kLgChunk * sizeof(int) + lg_gepp_smem<T>();
   const size_t tree_smem = lg_tree_smem<T>((n + kLgChunk - 1) / kLgChunk);
   void* tree_k = (void*)&lg_tree_kernel<T>;
@@ -117,7 +161,7 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
         lg_coef_kernel<T, false><<<dim3((n - r_lo + 255) / 256, cnt), 256, 0, s>>>(A, r_lo);
       }
       const int u_lo = grad ? 0 : k0 + A.kw;
-      if (u_lo < n) lg_update_kernel<T><<<dim3((n - u_lo + 63) / 64, (n - u_lo + 63) / 64, cnt), 256, 0, s>>>(A, u_lo, u_lo);
+      if (int e = lg_update<T, false>(s, A, u_lo, cnt, J.prec)) return e;
     }
     lg_finish_kernel<T><<<cnt, 32, 0, s>>>(A, J, b0, grad ? 1 : 0);
     if (grad) {
@@ -177,6 +221,7 @@ int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
   U.C = A.C;
   U.P = A.P;
   U.n = n;
+  U.wait_polls = J.wait_polls;
   // n <= 512: 512-row panel blocks with twice the pairs (a wider, less memory-bound update)
   const bool small = n <= 512;
   constexpr int NPS = PflCfg<T>::NP_SMALL;
@@ -215,7 +260,7 @@ int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
       if (lo < n) {
         U.k0 = k0;
         U.kw = 2 * A.np;
-        lg_update_kernel<T, true><<<dim3((n - lo + 63) / 64, (n - lo + 63) / 64, cnt), 256, 0, s>>>(U, lo, lo);
+        if (int e = lg_update<T, true>(s, U, lo, cnt, J.prec)) return e;
       }
     }
     pfl_finish_kernel<T><<<cnt, 32, 0, s>>>(A, J, b0);
