@@ -283,8 +283,9 @@ def run_move(a, rank, world, local):
     kind = {"f32": 0, "f64": 1, "c64": 2, "c128": 3}[a.dtype]
     B, n, k = a.batch, a.n, a.move
     pfm = a.op == "slogpf"
-    if pfm and (k != 1 or n % 2):
-        raise SystemExit("Pfaffian moves (--op slogpf) need --move 1 and an even n")
+    if pfm and n % 2:
+        raise SystemExit("Pfaffian moves (--op slogpf) need an even n")
+    pfk = pfm and k > 1  # k-index Pfaffian move (three passes over G)
     gen = torch.Generator(device=dev)
     gen.manual_seed(a.seed + 1000 * rank)
     # G of a well-conditioned matrix (identity-shifted A, or a skew S shifted by pair blocks
@@ -297,7 +298,7 @@ def run_move(a, rank, world, local):
         J[r, r + 1], J[r + 1, r] = 2.0, -2.0
         A = A - A.transpose(-1, -2) + J
         G = (0.5 * torch.linalg.inv(A).transpose(-1, -2)).contiguous()
-        IDX = torch.randint(0, n, (B, 1), generator=gen, device=dev, dtype=torch.int32)
+        IDX = torch.rand((B, n), generator=gen, device=dev).argsort(dim=1)[:, :k].to(torch.int32).contiguous()
     else:
         A = A + 2 * torch.eye(n, device=dev)
         G = torch.linalg.inv(A).transpose(-1, -2).contiguous()
@@ -307,13 +308,18 @@ def run_move(a, rank, world, local):
     del A
     sign = torch.empty(B, dtype=tdt, device=dev)
     logabs = torch.empty(B, dtype=rdt, device=dev)
-    wsb = (L.fermix_slogpf_update_workspace_bytes(kind, B, n) if pfm else
+    wsb = (L.fermix_slogpf_move_k_workspace_bytes(kind, B, n, k) if pfk else
+           L.fermix_slogpf_update_workspace_bytes(kind, B, n) if pfm else
            L.fermix_slogdet_update_workspace_bytes(kind, B, n, k))
     ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
 
     def call(Ud, Id):
+        if pfk:
+            _lib.check(L.fermix_slogpf_update_k(sp, kind, B, n, k, G.data_ptr(), Ud.data_ptr(), Id.data_ptr(), None,
+                                                sign.data_ptr(), logabs.data_ptr(), ws.data_ptr(), wsb))
+            return
         if pfm:
             _lib.check(L.fermix_slogpf_update(sp, kind, B, n, G.data_ptr(), Ud.data_ptr(), Id.data_ptr(), None,
                                               sign.data_ptr(), logabs.data_ptr(), ws.data_ptr(), wsb))
@@ -350,7 +356,8 @@ def run_move(a, rank, world, local):
     t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     ck = clocks.stop()
     s = G.element_size()
-    by = 2 * n * n * s + k * n * s + k * 4  # G read + written, the new rows, the indices
+    # G read + written (k-index Pfaffian move: read twice), the new rows, the indices
+    by = (3 if pfk else 2) * n * n * s + k * n * s + k * 4
     launch_s = t_dev / a.steps  # both kernels of the call: an upper bound on the row kernel's time
     hbm, peak_kind = peaks()
     achieved = B * by / launch_s / 1e9
@@ -396,7 +403,9 @@ def run_move(a, rank, world, local):
         threads = os.cpu_count() or 1
         with threadpool_limits(limits=threads):
             t0 = time.perf_counter()
-            if pfm:
+            if pfk:
+                moves.pf_update_woodbury_k(Gh, Uh, Ih)
+            elif pfm:
                 moves.pf_update_woodbury(Gh, Uh[:, 0], Ih[:, 0])
             else:
                 moves.ratio_woodbury(Gh, Uh, Ih)
@@ -406,7 +415,8 @@ def run_move(a, rank, world, local):
                "sample": f"{cnt} moves of the same workload ({dt:.2f} s; numpy Woodbury ratio + update in float64)"}
     if rank == 0:
         line = {
-            "metric": ("one-index Pfaffian moves/sec (ratio + in-place gradient update)" if pfm else
+            "metric": (f"{k}-index Pfaffian moves/sec (ratio + in-place gradient update)" if pfk else
+                       "one-index Pfaffian moves/sec (ratio + in-place gradient update)" if pfm else
                        "k-row determinant moves/sec (ratio + in-place inverse update)"),
             "value": world * B * a.steps / t_dev,
             "unit": "moves/s",
@@ -419,19 +429,20 @@ def run_move(a, rank, world, local):
             "vs_baseline": None,
             "dtype": a.dtype,
             "data": "synthetic (seeded G = inv(A)^T of A ~ N(0, 1/n) + 2I, new rows near the replaced ones)",
-            "config": {"workload": (f"slogpf one-index move {a.dtype} B={B}/GPU n={n}" if pfm else
+            "config": {"workload": (f"slogpf {k}-index move {a.dtype} B={B}/GPU n={n}" if pfk else
+                                    f"slogpf one-index move {a.dtype} B={B}/GPU n={n}" if pfm else
                                     f"slogdet {k}-row move {a.dtype} B={B}/GPU n={n}"),
                        "op": "slogpf_update" if pfm else "slogdet_update",
                        "batch_per_gpu": B, "n": n, "k": k, "parallelism": f"batch sharded x{world}, no collective",
                        "l2": "G exceeds L2 (no flush needed)" if B * n * n * s > 126e6 else "G fits L2"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "pfm_rows_kernel" if pfm else "upd_rows_vec_kernel",
+                         "kernel": "pfk_rows_kernel" if pfk else "pfm_rows_kernel" if pfm else "upd_rows_vec_kernel",
                          "timing": "the whole call (ratio kernel + row kernel): an upper bound on the row kernel's time",
                          "algorithmic_bytes_per_launch": B * by},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": a.steps * (3 if pfm else 2),
+            "gpu_launches": a.steps * (3 if pfm else 2),  # pfk: v, prep, rows; pfm: ratio, v, rows
             "clocks": ck,
         }
         print(json.dumps(line), flush=True)

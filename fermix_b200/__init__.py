@@ -17,7 +17,9 @@ from .api import (
     slogdet_ratio,
     slogdet_update,
     slogpf_ratio,
+    slogpf_ratio_k,
     slogpf_update,
+    slogpf_update_k,
     slogdet_parts,
     slogdet_planar,
     slogpf,
@@ -42,6 +44,8 @@ __all__ = [
     "slogdet_update",
     "slogpf_ratio",
     "slogpf_update",
+    "slogpf_ratio_k",
+    "slogpf_update_k",
     "slogdet_planar",
     "slogpf_planar",
     "det_planar",

@@ -35,6 +35,9 @@ SIGNATURES = {
     "fermix_slogpf_ratio": (_i, [_vp, _i, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "fermix_slogpf_update": (_i, [_vp, _i, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz]),
     "fermix_slogpf_update_workspace_bytes": (_sz, [_i, _i64, _i64]),
+    "fermix_slogpf_ratio_k": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _sz]),
+    "fermix_slogpf_update_k": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz]),
+    "fermix_slogpf_move_k_workspace_bytes": (_sz, [_i, _i64, _i64, _i64]),
     "fermix_workspace_bytes": (_sz, [_i, _i, _i64, _i64, _i]),
     "fermix_check_prec": (_i, [_i, _i]),
     "fermix_strerror": (ctypes.c_char_p, [_i]),

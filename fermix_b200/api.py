@@ -580,6 +580,68 @@ def slogpf_update(g, row, idx, *, accept=None, inplace=False):
     return sign.reshape(batch), logabs.reshape(batch), (g if inplace else G.reshape(g.shape))
 
 
+def _pf_move_k_args(g, rows, idx):
+    """Checks of the k-index Pfaffian move functions: g (..., n, n), rows (..., k, n), idx (..., k)."""
+    g, U, I, batch, B, n, k = _move_args(g, rows, idx)
+    if n < 2:
+        raise ValueError("a Pfaffian move needs n >= 2")
+    return g, U, I, batch, B, n, k
+
+
+def slogpf_ratio_k(g, rows, idx):
+    """Pfaffian ratio of a k-index move (no reference counterpart: the multi-electron move
+    of a Pfaffian wavefunction). ``g`` (..., n, n) holds S^-T / 2 -- the gradient
+    ``slogpf_parts`` returns -- and the move replaces rows ``idx`` (..., k) of the skew S by
+    ``rows`` (..., k, n) and the same columns by -rows, applied in order (k one-index moves;
+    on the idx x idx block the later row wins). Returns (sign, logabs) of pf(S') / pf(S) in
+    the slogpf conventions; reads all of each g once."""
+    g, U, I, batch, B, n, k = _pf_move_k_args(g, rows, idx)
+    G = g.detach().reshape(B, n, n).contiguous()
+    sign = torch.empty(B, dtype=g.dtype, device=g.device)
+    logabs = torch.empty(B, dtype=_real(g.dtype), device=g.device)
+    L = _lib.lib()
+    kind = _KIND[g.dtype]
+    with torch.cuda.device(g.device):
+        nb = L.fermix_slogpf_move_k_workspace_bytes(kind, B, n, k)
+        ws = torch.empty(nb, dtype=torch.uint8, device=g.device) if nb else None
+        st = L.fermix_slogpf_ratio_k(_stream_ptr(g.device), kind, B, n, k, _ptr(G), _ptr(U), _ptr(I), _ptr(sign),
+                                     _ptr(logabs), _ptr(ws), nb)
+    _lib.check(st)
+    return sign.reshape(batch), logabs.reshape(batch)
+
+
+def slogpf_update_k(g, rows, idx, *, accept=None, inplace=False):
+    """Apply a k-index Pfaffian move to the gradient: as ``slogpf_ratio_k``, and also
+    g <- S'^-T / 2 where ``accept`` (bool, shape g.shape[:-2]; None = all) is true; the
+    others keep g. A member whose ratio is exactly 0 gets a zero matrix. Returns
+    (sign, logabs, g_new); with ``inplace=True`` g (a contiguous CUDA tensor) is updated
+    and returned. Not differentiable."""
+    g, U, I, batch, B, n, k = _pf_move_k_args(g, rows, idx)
+    if inplace:
+        if not g.is_contiguous():
+            raise ValueError("inplace=True needs a contiguous g")
+        G = g.detach().view(B, n, n)
+    else:
+        G = g.detach().reshape(B, n, n).clone()
+    acc = None
+    if accept is not None:
+        acc = torch.as_tensor(accept, device=g.device)
+        if tuple(acc.shape) != batch:
+            raise ValueError(f"accept must have shape {batch}, got {tuple(acc.shape)}")
+        acc = acc.to(torch.uint8).reshape(B).contiguous()
+    sign = torch.empty(B, dtype=g.dtype, device=g.device)
+    logabs = torch.empty(B, dtype=_real(g.dtype), device=g.device)
+    L = _lib.lib()
+    kind = _KIND[g.dtype]
+    with torch.cuda.device(g.device):
+        nb = L.fermix_slogpf_move_k_workspace_bytes(kind, B, n, k)
+        ws = torch.empty(nb, dtype=torch.uint8, device=g.device) if nb else None
+        st = L.fermix_slogpf_update_k(_stream_ptr(g.device), kind, B, n, k, _ptr(G), _ptr(U), _ptr(I), _ptr(acc),
+                                      _ptr(sign), _ptr(logabs), _ptr(ws), nb)
+    _lib.check(st)
+    return sign.reshape(batch), logabs.reshape(batch), (g if inplace else G.reshape(g.shape))
+
+
 def slogdet(a, *, prec=None, unroll_steps=None, block=None):
     """Sign and log|det| of a batch of matrices ``a`` of shape (..., n, n)
     (src/fermix/api.py:148-174). Returns (sign, logabsdet): sign has the dtype of ``a``

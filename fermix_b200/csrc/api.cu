@@ -665,6 +665,47 @@ size_t fermix_slogpf_update_workspace_bytes(int dtype, int64_t batch, int64_t n)
   }) * 256);
 }
 
+int fermix_slogpf_ratio_k(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, const void* g,
+                          const void* rows, const int* idx, void* sign, void* logabs, void* workspace,
+                          size_t workspace_bytes) {
+  int e = upd_validate(dtype, batch, n, k);
+  if (e) return e;
+  if (n < 2) return FX_ERR_SHAPE;
+  if (batch == 0) return FX_OK;
+  if ((k > 0 && (!g || !rows || !idx)) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_pf_move_k<T>(s, batch, n, k, const_cast<void*>(g), rows, idx, nullptr, sign, logabs, workspace,
+                            workspace_bytes, false);
+  });
+}
+
+int fermix_slogpf_update_k(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, void* g, const void* rows,
+                           const int* idx, const unsigned char* accept, void* sign, void* logabs, void* workspace,
+                           size_t workspace_bytes) {
+  int e = upd_validate(dtype, batch, n, k);
+  if (e) return e;
+  if (n < 2) return FX_ERR_SHAPE;
+  if (batch == 0) return FX_OK;
+  if ((k > 0 && (!g || !rows || !idx)) || !sign || !logabs) return FX_ERR_NULL;
+  align_workspace(workspace, workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return by_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    return run_pf_move_k<T>(s, batch, n, k, g, rows, idx, accept, sign, logabs, workspace, workspace_bytes, true);
+  });
+}
+
+size_t fermix_slogpf_move_k_workspace_bytes(int dtype, int64_t batch, int64_t n, int64_t k) {
+  if (upd_validate(dtype, batch, n, k) || batch == 0 || n < 2) return 0;
+  return with_slack((size_t)by_dtype(dtype, [&](auto t) -> int {
+    using T = decltype(t);
+    return (int)((pfk_ws_bytes<T>(batch, n, k) + 255) / 256);
+  }) * 256);
+}
+
 int fermix_slogdet_ratio(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, const void* g,
                          const void* rows, const int* idx, void* sign, void* logabs) {
   int e = upd_validate(dtype, batch, n, k);

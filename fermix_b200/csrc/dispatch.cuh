@@ -119,6 +119,12 @@ template <typename T>
 int run_pf_move(cudaStream_t s, int64_t batch, int64_t n, void* g, const void* u, const int* idx,
                 const unsigned char* accept, void* sign, void* logabs, void* ws, size_t wsb, bool apply);
 
+template <typename T>
+size_t pfk_ws_bytes(int64_t batch, int64_t n, int64_t k);
+template <typename T>
+int run_pf_move_k(cudaStream_t s, int64_t batch, int64_t n, int64_t k, void* g, const void* u, const int* idx,
+                  const unsigned char* accept, void* sign, void* logabs, void* ws, size_t wsb, bool apply);
+
 }  // namespace fxh
 
 // Explicit instantiation of a launcher template for the four dtypes.

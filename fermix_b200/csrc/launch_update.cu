@@ -2,6 +2,7 @@
 // and launches.
 #include "dispatch.cuh"
 #include "update.cuh"
+#include "update_pfk.cuh"
 
 namespace fxh {
 
@@ -198,6 +199,55 @@ int run_pf_move(cudaStream_t s, int64_t batch, int64_t n, void* g, const void* u
   return FX_OK;
 }
 
+// Workspace of the k-index Pfaffian move: the action (B ints), 1 / rho (B x k), then V, g_t
+// and y_t (B x k x n each).
+template <typename T>
+size_t pfk_ws_bytes(int64_t batch, int64_t n, int64_t k) {
+  return align256((size_t)batch * sizeof(int)) + align256((size_t)batch * k * sizeof(T)) +
+         3 * align256((size_t)batch * k * n * sizeof(T));
+}
+
+// k-index Pfaffian move: ratio only (apply == false) or ratio plus the in-place update
+template <typename T>
+int run_pf_move_k(cudaStream_t s, int64_t batch, int64_t n, int64_t k, void* g, const void* u, const int* idx,
+                  const unsigned char* accept, void* sign, void* logabs, void* ws, size_t wsb, bool apply) {
+  const DevInfo* D = dev_info();
+  if (!D) return FX_ERR_DEVICE;
+  if (!ws || wsb < pfk_ws_bytes<T>(batch, n, k)) return FX_ERR_WORKSPACE;
+  PfkArgs<T> A;
+  A.g = static_cast<T*>(g);
+  A.u = static_cast<const T*>(u);
+  A.idx = idx;
+  A.accept = accept;
+  A.sign = static_cast<T*>(sign);
+  A.logabs = static_cast<typename Sc<T>::R*>(logabs);
+  A.B = batch;
+  A.n = (int)n;
+  A.k = (int)k;
+  unsigned char* p = static_cast<unsigned char*>(ws);
+  A.act = reinterpret_cast<int*>(p);
+  p += align256((size_t)batch * sizeof(int));
+  A.rinv = reinterpret_cast<T*>(p);
+  p += align256((size_t)batch * k * sizeof(T));
+  A.v = reinterpret_cast<T*>(p);
+  p += align256((size_t)batch * k * n * sizeof(T));
+  A.gv = reinterpret_cast<T*>(p);
+  p += align256((size_t)batch * k * n * sizeof(T));
+  A.yv = reinterpret_cast<T*>(p);
+  const int64_t wpb = kUpdRowThreads / 32, cap = (int64_t)D->sms * 8;
+  const int64_t gr = (batch * n + wpb - 1) / wpb;
+  pfk_v_kernel<T><<<(unsigned)(gr < cap ? gr : cap), kUpdRowThreads, 0, s>>>(A);
+  if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  const int64_t pcap = (int64_t)D->sms * 8;
+  pfk_prep_kernel<T><<<(unsigned)(batch < pcap ? batch : pcap), kPfkPrepThreads, 0, s>>>(A);
+  if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  if (apply) {
+    pfk_rows_kernel<T><<<(unsigned)(gr < cap ? gr : cap), kUpdRowThreads, 0, s>>>(A);
+    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  }
+  return FX_OK;
+}
+
 int update_status(int clear) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, umma::fx_status_word, sizeof(int)) != cudaSuccess) return -1;
@@ -214,7 +264,10 @@ int update_status(int clear) {
                              const unsigned char*, void*, void*, void*, size_t, bool);                    \
   template size_t pfm_ws_bytes<T>(int64_t, int64_t);                                                      \
   template int run_pf_move<T>(cudaStream_t, int64_t, int64_t, void*, const void*, const int*,             \
-                              const unsigned char*, void*, void*, void*, size_t, bool);
+                              const unsigned char*, void*, void*, void*, size_t, bool);                   \
+  template size_t pfk_ws_bytes<T>(int64_t, int64_t, int64_t);                                             \
+  template int run_pf_move_k<T>(cudaStream_t, int64_t, int64_t, int64_t, void*, const void*, const int*,  \
+                                const unsigned char*, void*, void*, void*, size_t, bool);
 FXH_FOR_REAL(FXH_INST)
 FXH_FOR_COMPLEX(FXH_INST)
 

@@ -46,12 +46,11 @@ struct PfTcSmem {
   __align__(16) float zp[16][20];        // Z = W_P^-1, row k from pivot row k
   uint4 pcand[4];                        // per-warp pivot candidates: key, row, -, value bits
   int cand_f[4];                         // scratch (the singular flag at the end)
-  int at[kTcN], pof[kTcN];               // position -> row, row -> position (virtual pivoting)
+  int at[kTcN];                          // position -> row (virtual pivoting)
   int pidx[16];                          // the panel's pivot rows a_0, p_0, a_1, p_1, ...
-  unsigned char isP[kTcN];
   float dvec[kTcN / 2];
   uint32_t tslot;
-  int parity, bad;
+  int bad;
   uint64_t mbar;
 };
 static_assert(offsetof(PfTcSmem, v) == offsetof(PfTcSmem, u) + sizeof(float) * 8 * kTcN, "u, v contiguous");
@@ -87,12 +86,10 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
     if (tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
     tc_load_matrix(src, n, J.skew != 0, trow, x);
     S.at[x] = x;
-    S.pof[x] = x;
-    S.isP[x] = 0;
-    if (tid == 0) {
-      S.parity = 0;
-      S.bad = 0;
-    }
+    if (tid == 0) S.bad = 0;
+    // virtual pivoting: each thread tracks its own row's position; every thread keeps the
+    // interchange parity (all see the same pivots)
+    int pos = x, par = 0;
     bool live = x < n;
     tc_sync();
     FX_TOC(tq, 8);
@@ -102,6 +99,7 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
       const int np = min(8, npairs - g0);
       const bool swept_before = !live && x < n;
       float ur[8], vr[8], dr[8];
+      int kx = -1;  // this row's slot among the panel's pivot rows (a_t -> 2 t, p_t -> 2 t + 1)
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         ur[t] = vr[t] = dr[t] = 0.f;
@@ -114,65 +112,77 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
           if (x == a) live = false;
           // column a of the current matrix: stale TMEM value plus this panel's corrections
           float colA = __uint_as_float(umma::tmem_ld1(trow + a));
-          umma::tmem_wait_ld();
+          {
+            // this panel's corrections in two independent FMA chains (u and v terms)
+            float cu = 0.f, cv = 0.f;
 #pragma unroll
-          for (int t = 0; t < 8; ++t)
-            if (t < s) {
-              const float r1 = dr[t] * S.v[t][a], r2 = -dr[t] * S.u[t][a];
-              colA = fmaf(-ur[t], r1, colA);
-              colA = fmaf(-vr[t], r2, colA);
-            }
+            for (int t = 0; t < 8; ++t)
+              if (t < s) {
+                cu = fmaf(ur[t], dr[t] * S.v[t][a], cu);
+                cv = fmaf(vr[t], -dr[t] * S.u[t][a], cv);
+              }
+            umma::tmem_wait_ld();
+            colA -= cu + cv;
+          }
           // pivot: largest |colA| over the unassigned rows (first occurrence): per warp two
           // redux.sync on the packed key, then the four warps' candidates
           const unsigned key = piv_key(colA, live);
           const unsigned km = __reduce_max_sync(0xffffffffu, key);
           const int wi = __reduce_min_sync(0xffffffffu, key == km ? x : 0x7fffffff);
-          if (x == wi) S.pcand[warp] = make_uint4(km, (unsigned)wi, 0u, __float_as_uint(colA));
+          if (x == wi) S.pcand[warp] = make_uint4(km, (unsigned)wi, (unsigned)pos, __float_as_uint(colA));
           __syncthreads();
           uint4 hd[4];
 #pragma unroll
           for (int w = 0; w < 4; ++w) hd[w] = S.pcand[w];
-          unsigned bk = hd[0].x, bp = hd[0].y, bvb = hd[0].w;
+          unsigned bk = hd[0].x, bp = hd[0].y, bq = hd[0].z, bvb = hd[0].w;
 #pragma unroll
           for (int w = 1; w < 4; ++w)
             if (hd[w].x > bk || (hd[w].x == bk && hd[w].y < bp)) {
               bk = hd[w].x;
               bp = hd[w].y;
+              bq = hd[w].z;
               bvb = hd[w].w;
             }
-          const int p = (int)bp;
+          const int p = (int)bp, q = (int)bq;  // the pivot row and its position
           const float d = -__uint_as_float(bvb);  // all candidates NaN: the first one, d = NaN
           const float inv = d == 0.f ? 0.f : __fdiv_rn(1.f, d);
           if (x == p) live = false;
           float colP = __uint_as_float(umma::tmem_ld1(trow + p));
-          umma::tmem_wait_ld();
+          {
+            float cu = 0.f, cv = 0.f;
 #pragma unroll
-          for (int t = 0; t < 8; ++t)
-            if (t < s) {
-              const float r1 = dr[t] * S.v[t][p], r2 = -dr[t] * S.u[t][p];
-              colP = fmaf(-ur[t], r1, colP);
-              colP = fmaf(-vr[t], r2, colP);
-            }
+            for (int t = 0; t < 8; ++t)
+              if (t < s) {
+                cu = fmaf(ur[t], dr[t] * S.v[t][p], cu);
+                cv = fmaf(vr[t], -dr[t] * S.u[t][p], cv);
+              }
+            umma::tmem_wait_ld();
+            colP -= cu + cv;
+          }
           ur[s] = colP * inv;
           vr[s] = -colA * inv;
           dr[s] = d;
           S.u[s][x] = ur[s];
           S.v[s][x] = vr[s];
-          if (tid == 0) {
-            const int q = S.pof[p];
-            if (q != c + 1) {
-              const int y = S.at[c + 1];
+          // the interchange of positions c + 1 and q, written by the two rows involved
+          if (q != c + 1) {
+            par ^= 1;
+            if (x == p) {
               S.at[c + 1] = p;
-              S.at[q] = y;
-              S.pof[p] = c + 1;
-              S.pof[y] = q;
-              S.parity ^= 1;
+              pos = c + 1;
+            } else if (pos == c + 1) {
+              S.at[q] = x;
+              pos = q;
             }
+          }
+          if (x == p) {
             S.dvec[g0 + s] = d;
-            S.pidx[2 * s] = a;
             S.pidx[2 * s + 1] = p;
-            S.isP[a] = 1;
-            S.isP[p] = 1;
+            kx = 2 * s + 1;
+          }
+          if (x == a) {
+            S.pidx[2 * s] = a;
+            kx = 2 * s;
           }
           __syncthreads();
         }
@@ -180,11 +190,7 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
       FX_TOC(tq, 9);
       // ---- gradient mode: pivot row k publishes its row of W_P, the multipliers of the
       // earlier pairs (its own pair's identity block and the zero upper part are implied)
-      int kx = -1;
       if (GRAD) {
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-          if (k < 2 * np && S.pidx[k] == x) kx = k;
         if (kx >= 0) {
           const int kb = kx & ~1;
           float4* w4 = reinterpret_cast<float4*>(S.wp[kx]);
@@ -365,8 +371,6 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
         tc_sync();
         FX_TOC(tq, 4);
       }
-      // the panel's pivots are swept now
-      S.isP[x] = 0;
       __syncthreads();
       FX_TOC(tq, 12);
     }
@@ -391,7 +395,7 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
         nz += __shfl_xor_sync(0xffffffffu, nz, off);
       }
       if (lane == 0) {
-        if (S.parity) sg = -sg;
+        if (par) sg = -sg;
         if (nz) sg = 0.f;
         const float la = nz ? -INFINITY : lsum;
         J.sign[b] = S.bad ? __int_as_float(0x7fc00000) : sg;

@@ -174,6 +174,29 @@ int fermix_slogpf_update(void* stream, int dtype, int64_t batch, int64_t n, void
                          size_t workspace_bytes);
 size_t fermix_slogpf_update_workspace_bytes(int dtype, int64_t batch, int64_t n);
 
+/* k-index Pfaffian move (no reference counterpart; the multi-electron move of a Pfaffian
+ * wavefunction, on the gradient fermix_slogpf_grad exports -- _pf_parts,
+ * src/fermix/_pfinv.py:196-269). g holds G = S^-T / 2 per matrix. The move replaces rows
+ * idx[b * k + r] (int32, distinct, in [0, n)) of the skew S by rows[b, r, :] ((batch, k, n))
+ * and the same columns by -rows[b, r, :], applied in order r = 0 .. k - 1: it is the
+ * composition of k one-index moves (on the idx x idx block the later row wins; rows[b, r,
+ * idx[b * k + r]] is ignored). 0 <= k <= 16, k <= n, n >= 2.
+ *   fermix_slogpf_ratio_k:  (sign, logabs) of pf(S') / pf(S), in the slogpf conventions
+ *                           ((0, -inf) when it is 0, NaN for an index outside [0, n)).
+ *                           Reads all of G once (the ratio depends on u_r^T G u_s).
+ *   fermix_slogpf_update_k: the same ratio, and G replaced in place by S'^-T / 2 for every
+ *                           matrix with accept[b] != 0 (accept NULL = all); a member whose
+ *                           ratio is exactly 0 gets G' = 0, one with a bad index keeps G.
+ *                           rows must not overlap g. G is read twice and written once.
+ * Both take a workspace of fermix_slogpf_move_k_workspace_bytes. */
+int fermix_slogpf_ratio_k(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, const void* g,
+                          const void* rows, const int* idx, void* sign, void* logabs, void* workspace,
+                          size_t workspace_bytes);
+int fermix_slogpf_update_k(void* stream, int dtype, int64_t batch, int64_t n, int64_t k, void* g, const void* rows,
+                           const int* idx, const unsigned char* accept, void* sign, void* logabs, void* workspace,
+                           size_t workspace_bytes);
+size_t fermix_slogpf_move_k_workspace_bytes(int dtype, int64_t batch, int64_t n, int64_t k);
+
 /* Size of the fixed device array fermix_slogdet_grad_static uses instead of a workspace
  * (16 MiB, one copy per device, part of the library's device image). */
 #define FX_STATIC_SCRATCH_BYTES (16u << 20)

@@ -128,3 +128,81 @@ def pf_update_woodbury(G, row, idx):
     np.put_along_axis(y, I[..., None], np.take_along_axis(y, I[..., None], -1) + 1, axis=-1)
     upd = np.einsum("...j,...c->...jc", y, gi) - np.einsum("...j,...c->...jc", gi, y)
     return G + upd / rho[..., None, None]
+
+
+# ---------------------------------------------------------------- k-index Pfaffian moves
+# A k-index move replaces rows idx[r] of the skew S by rows[r] and columns idx[r] by
+# -rows[r], applied in order r = 0 .. k-1 (so on the idx x idx block the later row wins;
+# rows[r][idx[r]] is ignored): it is the composition of k one-index moves.
+
+def pf_apply_move_k(S, rows, idx):
+    """S' of a k-index move (float64 / complex128), the one-index moves applied in order."""
+    S = _wide(S).copy()
+    B = S.reshape((-1,) + S.shape[-2:])
+    U = _wide(rows).reshape((B.shape[0],) + np.asarray(rows).shape[-2:])
+    I = np.asarray(idx).reshape(B.shape[0], -1)
+    for r in range(I.shape[1]):
+        B[:] = pf_apply_move(B, U[:, r], I[:, r])
+    return B.reshape(S.shape)
+
+
+def pf_ratio_direct_k(S, rows, idx):
+    """(sign, logabs) of pf(S') / pf(S) by refactoring both (float64 / complex128)."""
+    S = _wide(S)
+    s0, l0 = _slogpf(S)
+    s1, l1 = _slogpf(pf_apply_move_k(S, rows, idx))
+    return s1 / np.where(s0 == 0, 1, s0), l1 - l0
+
+
+def pf_grad_direct_k(S, rows, idx):
+    """S'^-T / 2 of a k-index move (float64 / complex128)."""
+    return 0.5 * np.swapaxes(np.linalg.inv(pf_apply_move_k(S, rows, idx)), -1, -2)
+
+
+def pf_factors_k(G, rows, idx):
+    """The k-index move from G = S^-T / 2 alone (float64 / complex128): with G_t the
+    gradient after t one-index moves, g_t = row idx[t] of G_t, rho_t = 2 g_t . u_t and
+    y_t = e_idx[t] - 2 G_t u_t, so that G_{t+1} = G_t + (y_t g_t^T - g_t y_t^T) / rho_t.
+    Every G_t u and every row of G_t follow from V = G U^T (one pass over G) and the rows
+    idx of G by the rank-2 corrections, O(n k^2). Returns (rho[B, k], g[B, k, n],
+    y[B, k, n]); the ratio is prod(rho) and G' = G + sum_t (y_t g_t^T - g_t y_t^T) / rho_t."""
+    G = _wide(G)
+    Bsh = G.shape[:-2]
+    n = G.shape[-1]
+    Gf = G.reshape(-1, n, n)
+    U = _wide(rows).reshape(Gf.shape[0], -1, n).copy()
+    I = np.asarray(idx).reshape(Gf.shape[0], -1)
+    k = I.shape[1]
+    for b in range(Gf.shape[0]):
+        for t in range(k):
+            U[b, t, I[b, t]] = 0  # u_t[idx_t] is ignored
+    V = np.einsum("bjc,btc->btj", Gf, U)  # V[t] = G u_t
+    rho = np.zeros((Gf.shape[0], k), dtype=G.dtype)
+    gs = np.zeros((Gf.shape[0], k, n), dtype=G.dtype)
+    ys = np.zeros((Gf.shape[0], k, n), dtype=G.dtype)
+    for b in range(Gf.shape[0]):
+        for t in range(k):
+            i = I[b, t]
+            g = Gf[b, i].copy()          # row i of G_t
+            w = V[b, t].copy()           # G_t u_t
+            for q in range(t):
+                yq, gq, rq = ys[b, q], gs[b, q], rho[b, q]
+                g += (yq[i] * gq - gq[i] * yq) / rq
+                w += (yq * (gq @ U[b, t]) - gq * (yq @ U[b, t])) / rq
+            rho[b, t] = 2 * (g @ U[b, t])
+            y = -2 * w
+            y[i] += 1
+            gs[b, t], ys[b, t] = g, y
+    return rho.reshape(Bsh + (k,)), gs.reshape(Bsh + (k, n)), ys.reshape(Bsh + (k, n))
+
+
+def pf_ratio_woodbury_k(G, rows, idx):
+    rho, _, _ = pf_factors_k(G, rows, idx)
+    return np.prod(rho, axis=-1)
+
+
+def pf_update_woodbury_k(G, rows, idx):
+    rho, g, y = pf_factors_k(G, rows, idx)
+    G = _wide(G)
+    upd = np.einsum("...tj,...tc->...jc", y / rho[..., None], g) - np.einsum("...tj,...tc->...jc", g / rho[..., None], y)
+    return G + upd

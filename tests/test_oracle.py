@@ -257,3 +257,30 @@ def test_pf_move_oracle_woodbury_matches_refactorisation(dtype, n):
     assert np.allclose(r / np.abs(r), s1, rtol=0, atol=1e-9)
     G1 = moves.pf_grad_direct(S, U, idx)
     assert np.abs(moves.pf_update_woodbury(G, U, idx) - G1).max() <= 1e-8 * np.abs(G1).max()
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.complex128])
+@pytest.mark.parametrize("n,k", [(6, 1), (10, 2), (16, 5), (24, 8)])
+def test_pf_move_k_recurrence_matches_refactorisation(dtype, n, k):
+    """The G-only k-index Pfaffian move (the CUDA kernels' algorithm) against refactoring
+    the moved matrix, and k = 1 against the one-index Woodbury route."""
+    from oracle import moves
+
+    rng = np.random.default_rng(n + 100 * k)
+    B = 4
+    S = rng.standard_normal((B, n, n))
+    if np.dtype(dtype).kind == "c":
+        S = S + 1j * rng.standard_normal((B, n, n))
+    S = S - np.swapaxes(S, -1, -2)
+    G = 0.5 * np.swapaxes(np.linalg.inv(S), -1, -2)
+    idx = np.stack([rng.choice(n, k, replace=False) for _ in range(B)])
+    U = rng.standard_normal((B, k, n)) + (1j * rng.standard_normal((B, k, n)) if np.dtype(dtype).kind == "c" else 0)
+    s, l = moves.pf_ratio_direct_k(S, U, idx)
+    rho = moves.pf_ratio_woodbury_k(G, U, idx)
+    assert np.abs(np.log(np.abs(rho)) - l).max() < 1e-9
+    assert np.abs(rho / np.abs(rho) - s).max() < 1e-9
+    ref = moves.pf_grad_direct_k(S, U, idx)
+    assert np.abs(moves.pf_update_woodbury_k(G, U, idx) - ref).max() / np.abs(ref).max() < 1e-9
+    if k == 1:
+        one = moves.pf_update_woodbury(G, U[:, 0], idx[:, 0])
+        assert np.abs(moves.pf_update_woodbury_k(G, U, idx) - one).max() / np.abs(one).max() < 1e-12
