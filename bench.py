@@ -78,6 +78,8 @@ def parse():
                          "default workload at N = 1")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-launch-count", action="store_true",
+                    help="skip counting kernel launches with the CUDA profiler (for runs under ncu)")
     a = ap.parse_args()
     d = ap.parse_args([])
     a.is_default = all(getattr(a, k) == getattr(d, k) for k in
@@ -740,7 +742,7 @@ def measure(a, ctx, cpu=True, e2e=True):
         "binding": "hbm" if t_hbm >= t_pipe else cr["pipe"],
         "binding_frac": max(t_hbm, t_pipe) / launch_s,
     }
-    launches, kernels = count_launches(step)
+    launches, kernels = (None, ["not counted (--no-launch-count)"]) if a.no_launch_count else count_launches(step)
 
     # ---- end to end through the C ABI with host buffers
     e2e_line = None

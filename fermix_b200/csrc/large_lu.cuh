@@ -121,19 +121,43 @@ __device__ __forceinline__ typename Sc<T>::R lg_key(T v, bool live) {
   return a != a ? R(-0.5) : a;  // NaN: a candidate only when every candidate is NaN
 }
 
+// Order key of a pivot candidate as 64 bits: 0 = not a candidate, 1 = NaN (a candidate
+// only when every candidate is NaN), else the bits of abs1(v) (a non-negative float orders as
+// its bit pattern) plus 2.
+template <typename T>
+__device__ __forceinline__ uint64_t lg_key64(T v, bool live) {
+  typedef typename Sc<T>::R R;
+  if (!live) return 0ull;
+  const R a = abs1(v);
+  if (a != a) return 1ull;
+  if constexpr (sizeof(R) == 8) return (uint64_t)__double_as_longlong(a) + 2ull;
+  else return (uint64_t)__float_as_uint(a) + 2ull;
+}
+
+// Warp argmax over (key, then the smallest pos) with redux.sync: every lane gets the
+// winning key and pos.
+__device__ __forceinline__ void lg_warp_argmax(uint64_t key, int pos, uint64_t& km, int& pm) {
+  const unsigned hi = (unsigned)(key >> 32), lo = (unsigned)key;
+  const unsigned mh = __reduce_max_sync(0xffffffffu, hi);
+  const unsigned ml = __reduce_max_sync(0xffffffffu, hi == mh ? lo : 0u);
+  km = ((uint64_t)mh << 32) | ml;
+  pm = __reduce_min_sync(0xffffffffu, key == km ? pos : 0x7fffffff);
+}
+
 // Partial pivoting on the panel columns [k0, k0 + kw) of up to 512 listed rows (thread i
 // holds row rows[i] in registers). Writes the kw pivot rows in order to out[]; with
-// want_lu also L11 / U11 and the pivots. Every block thread must call it.
+// want_lu also L11 / U11 and the pivots. Every block thread must call it. Per column: each
+// warp reduces its candidates with redux.sync, the warp winners go to shared memory with
+// their rows, and after one barrier every warp reduces the 16 warp winners the same way.
 template <typename T, int NB>
 __device__ void lg_gepp(const T* __restrict__ Mb, int n, int k0, int kw, const int* rows, int count, int* out,
                         T* L11, T* U11, T* pivs, bool want_lu, unsigned char* smem) {
-  typedef typename Sc<T>::R R;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int NW = kLgChunk / 32;
-  R* skey = reinterpret_cast<R*>(smem);                         // [2][NW]
-  int* spos = reinterpret_cast<int*>(skey + 2 * NW);            // [2][NW] row position
-  int* sidx = spos + 2 * NW;                                    // [2][NW] list index
-  T* srow = reinterpret_cast<T*>(sidx + 2 * NW + (2 * NW) % 4);  // [2][NW][NB]
+  unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem);  // [2][NW]
+  int* spos = reinterpret_cast<int*>(skey + 2 * NW);                        // [2][NW] row position
+  int* sidx = spos + 2 * NW;                                                // [2][NW] list index
+  T* srow = reinterpret_cast<T*>(sidx + 2 * NW + (2 * NW) % 4);             // [2][NW][NB]
   const bool have = tid < count;
   const int myrow = have ? rows[tid] : 0x7fffffff;
   T pr[NB];
@@ -144,41 +168,28 @@ __device__ void lg_gepp(const T* __restrict__ Mb, int n, int k0, int kw, const i
   for (int s = 0; s < NB; ++s) {
     if (s < kw) {
       const bool live = mystep < 0;
-      R bv = lg_key(pr[s], live);
-      int bp = live ? myrow : 0x7fffffff;
-      int bi = tid;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const R ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int op = __shfl_xor_sync(0xffffffffu, bp, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (ov > bv || (ov == bv && op < bp)) {
-          bv = ov;
-          bp = op;
-          bi = oi;
-        }
-      }
+      const uint64_t key = lg_key64(pr[s], live);
+      const int pos = live ? myrow : 0x7fffffff;
+      uint64_t wk;
+      int wp;
+      lg_warp_argmax(key, pos, wk, wp);
+      const unsigned win = __ballot_sync(0xffffffffu, key == wk && pos == wp);
       const int par = s & 1;
-      if (tid == bi) {
-        skey[par * NW + warp] = bv;
-        spos[par * NW + warp] = bp;
-        sidx[par * NW + warp] = bi;
+      if (lane == __ffs(win) - 1) {
+        skey[par * NW + warp] = wk;
+        spos[par * NW + warp] = wp;
+        sidx[par * NW + warp] = tid;
 #pragma unroll
         for (int t = 0; t < NB; ++t) srow[(par * NW + warp) * NB + t] = pr[t];
       }
       __syncthreads();
-      int w0 = 0;
-      R kv = skey[par * NW];
-      int kp = spos[par * NW];
-      for (int w = 1; w < NW; ++w) {
-        const R ov = skey[par * NW + w];
-        const int op = spos[par * NW + w];
-        if (ov > kv || (ov == kv && op < kp)) {
-          kv = ov;
-          kp = op;
-          w0 = w;
-        }
-      }
+      const uint64_t ck = lane < NW ? (uint64_t)skey[par * NW + lane] : 0ull;
+      const int cp = lane < NW ? spos[par * NW + lane] : 0x7fffffff;
+      uint64_t kv;
+      int kp;
+      lg_warp_argmax(ck, cp, kv, kp);
+      const unsigned wwin = __ballot_sync(0xffffffffu, lane < NW && ck == kv && cp == kp);
+      const int w0 = __ffs(wwin) - 1;
       const bool valid = kp != 0x7fffffff;  // false once fewer rows than steps remain
       const int wi = sidx[par * NW + w0];
       const T* u = srow + (par * NW + w0) * NB;
@@ -211,9 +222,8 @@ __device__ void lg_gepp(const T* __restrict__ Mb, int n, int k0, int kw, const i
 
 template <typename T>
 constexpr size_t lg_gepp_smem() {
-  typedef typename Sc<T>::R R;
   constexpr int NW = kLgChunk / 32;
-  return 2 * NW * sizeof(R) + 4 * NW * sizeof(int) + 64 + 2 * NW * LgCfg<T>::NB * sizeof(T) + 64;
+  return 2 * NW * sizeof(unsigned long long) + 4 * NW * sizeof(int) + 64 + 2 * NW * LgCfg<T>::NB * sizeof(T) + 64;
 }
 
 // 1. leaf: chunk blockIdx.x of the rows [k0, n) of matrix blockIdx.y
