@@ -236,15 +236,18 @@ int run_pf_move_k(cudaStream_t s, int64_t batch, int64_t n, int64_t k, void* g, 
   A.yv = reinterpret_cast<T*>(p);
   const int64_t wpb = kUpdRowThreads / 32, cap = (int64_t)D->sms * 8;
   const int64_t gr = (batch * n + wpb - 1) / wpb;
-  pfk_v_kernel<T><<<(unsigned)(gr < cap ? gr : cap), kUpdRowThreads, 0, s>>>(A);
-  if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
+  const unsigned grid = (unsigned)(gr < 2 * cap ? gr : 2 * cap);  // two 256-thread blocks per SM, 8 waves
+  void* kv = k <= 2 ? (void*)&pfk_v_kernel<T, 2> : k <= 4 ? (void*)&pfk_v_kernel<T, 4>
+           : k <= 8 ? (void*)&pfk_v_kernel<T, 8> : (void*)&pfk_v_kernel<T, 16>;
+  void* kr = k <= 2 ? (void*)&pfk_rows_kernel<T, 2> : k <= 4 ? (void*)&pfk_rows_kernel<T, 4>
+           : k <= 8 ? (void*)&pfk_rows_kernel<T, 8> : (void*)&pfk_rows_kernel<T, 16>;
+  void* args[] = {&A};
+  if (cudaLaunchKernel(kv, dim3(grid), dim3(kUpdRowThreads), args, 0, s) != cudaSuccess) return FX_ERR_CUDA;
   const int64_t pcap = (int64_t)D->sms * 8;
   pfk_prep_kernel<T><<<(unsigned)(batch < pcap ? batch : pcap), kPfkPrepThreads, 0, s>>>(A);
   if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
-  if (apply) {
-    pfk_rows_kernel<T><<<(unsigned)(gr < cap ? gr : cap), kUpdRowThreads, 0, s>>>(A);
-    if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
-  }
+  if (apply && cudaLaunchKernel(kr, dim3(grid), dim3(kUpdRowThreads), args, 0, s) != cudaSuccess)
+    return FX_ERR_CUDA;
   return FX_OK;
 }
 

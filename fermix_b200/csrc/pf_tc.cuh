@@ -98,11 +98,11 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
     for (int g0 = 0; g0 < npairs; g0 += 8) {
       const int np = min(8, npairs - g0);
       const bool swept_before = !live && x < n;
-      float ur[8], vr[8], dr[8];
+      float ur[8], vr[8], dr[8], ir[8];  // ir[t] = 1 / d_t (0 for d_t = 0)
       int kx = -1;  // this row's slot among the panel's pivot rows (a_t -> 2 t, p_t -> 2 t + 1)
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
-        ur[t] = vr[t] = dr[t] = 0.f;
+        ur[t] = vr[t] = dr[t] = ir[t] = 0.f;
       }
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
@@ -162,6 +162,7 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
           ur[s] = colP * inv;
           vr[s] = -colA * inv;
           dr[s] = d;
+          ir[s] = inv;
           S.u[s][x] = ur[s];
           S.v[s][x] = vr[s];
           // the interchange of positions c + 1 and q, written by the two rows involved
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
             if (t < np && 2 * t + 1 >= kx) {
-              const float id = dr[t] == 0.f ? 0.f : __fdiv_rn(1.f, dr[t]);
+              const float id = ir[t];
               const float za = S.zp[2 * t][kx] * id, zb = S.zp[2 * t + 1][kx] * id;
               const float4* r0 = reinterpret_cast<const float4*>(S.zp[2 * t]);
               const float4* r1 = reinterpret_cast<const float4*>(S.zp[2 * t + 1]);

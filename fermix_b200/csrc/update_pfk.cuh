@@ -41,9 +41,10 @@ struct PfkArgs {
 
 constexpr int kPfkPrepThreads = 128;
 
-// V[t][j] = G_j . u_t, u_t with entry idx_t left out
-template <typename T>
-__global__ void __launch_bounds__(kUpdRowThreads) pfk_v_kernel(PfkArgs<T> A) {
+// V[t][j] = G_j . u_t, u_t with entry idx_t left out; KM (a power of two >= k) bounds the
+// unrolled coefficient loops
+template <typename T, int KM>
+__global__ void __launch_bounds__(kUpdRowThreads, 2) pfk_v_kernel(PfkArgs<T> A) {
   const int lane = threadIdx.x & 31;
   const int n = A.n, k = A.k;
   const int64_t nw = (int64_t)gridDim.x * (kUpdRowThreads / 32);
@@ -53,16 +54,20 @@ __global__ void __launch_bounds__(kUpdRowThreads) pfk_v_kernel(PfkArgs<T> A) {
     const T* gj = A.g + (b * n + j) * (int64_t)n;
     const T* ub = A.u + b * (int64_t)k * n;
     const int* ib = A.idx + b * k;
-    T acc[kUpdMaxK];
+    int id[KM];
 #pragma unroll
-    for (int t = 0; t < kUpdMaxK; ++t) acc[t] = s_zero<T>();
+    for (int t = 0; t < KM; ++t) id[t] = t < k ? ib[t] : -1;
+    T acc[KM];
+#pragma unroll
+    for (int t = 0; t < KM; ++t) acc[t] = s_zero<T>();
+#pragma unroll 1
     for (int c = lane; c < n; c += 32) {
       const T gv = gj[c];
 #pragma unroll
-      for (int t = 0; t < kUpdMaxK; ++t)
-        if (t < k && c != ib[t]) acc[t] = fma_(gv, ub[(int64_t)t * n + c], acc[t]);
+      for (int t = 0; t < KM; ++t)
+        if (t < k && c != id[t]) acc[t] = fma_(gv, ub[(int64_t)t * n + c], acc[t]);
     }
-    const T s = warp_reduce_scatter<T, kUpdMaxK>(acc, lane);
+    const T s = warp_reduce_scatter<T, KM>(acc, lane);
     if (lane < k) A.v[(b * k + lane) * (int64_t)n + j] = s;
   }
 }
@@ -195,9 +200,9 @@ __global__ void __launch_bounds__(kPfkPrepThreads) pfk_prep_kernel(PfkArgs<T> A)
   }
 }
 
-// G_j += sum_t (y_t[j] g_t - g_t[j] y_t) / rho_t; one warp per row
-template <typename T>
-__global__ void __launch_bounds__(kUpdRowThreads) pfk_rows_kernel(PfkArgs<T> A) {
+// G_j += sum_t (y_t[j] g_t - g_t[j] y_t) / rho_t; one warp per row; KM as pfk_v_kernel
+template <typename T, int KM>
+__global__ void __launch_bounds__(kUpdRowThreads, 2) pfk_rows_kernel(PfkArgs<T> A) {
   const int lane = threadIdx.x & 31;
   const int n = A.n, k = A.k;
   const int64_t nw = (int64_t)gridDim.x * (kUpdRowThreads / 32);
@@ -213,9 +218,9 @@ __global__ void __launch_bounds__(kUpdRowThreads) pfk_rows_kernel(PfkArgs<T> A) 
     }
     const T* gvb = A.gv + b * (int64_t)k * n;
     const T* yvb = A.yv + b * (int64_t)k * n;
-    T ca[kUpdMaxK], cb[kUpdMaxK];
+    T ca[KM], cb[KM];
 #pragma unroll
-    for (int t = 0; t < kUpdMaxK; ++t) {
+    for (int t = 0; t < KM; ++t) {
       ca[t] = cb[t] = s_zero<T>();
       if (t < k) {
         const T ri = A.rinv[b * k + t];
@@ -223,10 +228,11 @@ __global__ void __launch_bounds__(kUpdRowThreads) pfk_rows_kernel(PfkArgs<T> A) 
         cb[t] = mul(gvb[(int64_t)t * n + j], ri);
       }
     }
+#pragma unroll 1
     for (int c = lane; c < n; c += 32) {
       T x = gj[c];
 #pragma unroll
-      for (int t = 0; t < kUpdMaxK; ++t)
+      for (int t = 0; t < KM; ++t)
         if (t < k) x = fma_(ca[t], gvb[(int64_t)t * n + c], fms(x, cb[t], yvb[(int64_t)t * n + c]));
       gj[c] = x;
     }
