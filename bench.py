@@ -35,7 +35,8 @@ TC_KERNEL = {"slogpf": "pf_tc_kernel", "slogdet": "lu_tc_kernel"}
 def kernel_name(a):
     """The dominant kernel of this workload: the tensor-memory kernels for float32 /
     tf32x3 (slogpf 8 <= n <= 128, even n; slogdet 8 <= n <= 256), the register-panel
-    kernels otherwise up to n = 256, and above that the blocked engines' tiled update."""
+    kernels otherwise up to n = 256, and above that the blocked engines' trailing update
+    (tcgen05 for float32 / complex64 under tf32x3, DMMA for complex128, FMA tiles otherwise)."""
     if a.dtype == "f32" and a.prec == "tf32x3" and a.n >= 8:
         if a.op == "slogpf" and a.n <= 128 and a.n % 2 == 0:
             return TC_KERNEL[a.op]
@@ -43,7 +44,9 @@ def kernel_name(a):
             return TC_KERNEL[a.op]
     if a.n <= 256:
         return SMALL_KERNEL[a.op]
-    return "lg_update_kernel"
+    if a.dtype in ("f32", "c64") and a.prec == "tf32x3":
+        return "lg_tc_update_kernel"
+    return "lg_dmma_update_kernel" if a.dtype == "c128" else "lg_update_kernel"
 
 
 def parse():

@@ -176,3 +176,28 @@ def test_c5_c128_slogpf_fwd_grad_against_extended_precision(name):
         assert abs(complex(s[0].item()) - complex(pf_ref64(M)[0])) <= 1e-10
     R = 0.5 * torch.linalg.inv(x).transpose(-1, -2)
     assert float(_rel_rows(G, R[None])[0]) <= 1e-8
+
+
+def test_n8192_f64_slogdet_and_c128_slogpf_fwd_grad():
+    """The top of the large-n range (the slogpf forward's 8-block cluster panels): float64
+    slogdet and complex128 slogpf, forward and gradient, n = 8192, against fp64 LAPACK-class
+    references on the GPU (cuSOLVER through torch; their own error at this size is ~1e-11)."""
+    n = 8192
+    g = torch.Generator(device="cuda").manual_seed(8192)
+    A = torch.randn((1, n, n), generator=g, device="cuda", dtype=torch.float64)
+    s, l, G = fx.slogdet_parts(A)
+    s64, l64 = torch.linalg.slogdet(A)
+    assert torch.equal(s, s64)
+    assert abs(float(l[0] - l64[0])) <= 1e-9 * max(1.0, abs(float(l64[0])))
+    R = torch.linalg.inv(A).transpose(-1, -2)
+    assert float(_rel_rows(G, R)[0]) <= 1e-8
+    del A, G, R
+    C = torch.randn((1, n, n), generator=g, device="cuda", dtype=torch.complex128)
+    S = (C - C.transpose(-1, -2)).contiguous()
+    del C
+    s, l, G = fx.slogpf_parts(S, skew_symmetrize=False)
+    sd, ld = torch.linalg.slogdet(S)
+    assert abs(float(l[0] - 0.5 * ld[0])) <= 1e-9 * max(1.0, abs(float(ld[0])))
+    assert abs(complex(s[0].item()) ** 2 - complex(sd[0].item())) <= 1e-9
+    R = 0.5 * torch.linalg.inv(S).transpose(-1, -2)
+    assert float(_rel_rows(G, R)[0]) <= 1e-8
