@@ -540,7 +540,7 @@ def count_launches(fn, reps=3):
         with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
             for _ in range(reps):
                 fn()
-            torch.cuda.synchronize()
+                torch.cuda.synchronize()
         names = [e.name for e in prof.events() if e.device_type.name == "CUDA" and
                  not e.name.lower().startswith(("memcpy", "memset"))]
         if not names:

@@ -262,16 +262,25 @@ __global__ void __launch_bounds__(kLgChunk) lg_tree_kernel(LgArgs<T> A) {
     // this pass is plain partial pivoting
     for (int i = threadIdx.x; i < n - k0; i += blockDim.x) allc[i] = k0 + i;
     if (threadIdx.x == 0) *ntot = n - k0;
-  } else if (threadIdx.x == 0) {
-    int m = 0;
-    for (int i = 0; i < A.nchunk * kw; ++i) {
-      const int r = cb[(i / kw) * NB + i % kw];
-      if (r >= 0) allc[m++] = r;
-    }
-    *ntot = m;
   }
   __syncthreads();
-  const int total = *ntot;
+  int total = 0;
+  if (A.nchunk == 1) {
+    total = *ntot;
+  } else {
+    // the leaves' pivot rows in chunk order; every chunk but the last has 512 rows and always
+    // yields kw of them, and a chunk's valid entries come first (-1 once its rows run out), so
+    // the valid candidates form a prefix of the list: copy in parallel and count them
+    for (int base = 0; base < A.nchunk * kw; base += blockDim.x) {
+      const int i = base + threadIdx.x;
+      int r = -1;
+      if (i < A.nchunk * kw) {
+        r = cb[(i / kw) * NB + i % kw];
+        allc[i] = r;
+      }
+      total += __syncthreads_count(r >= 0);
+    }
+  }
   int count = min(total, kLgChunk);
   for (int i = threadIdx.x; i < count; i += blockDim.x) rows[i] = allc[i];
   int consumed = count;
