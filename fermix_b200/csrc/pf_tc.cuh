@@ -35,7 +35,8 @@
 namespace fx {
 
 struct PfTcSmem {
-  // u_t[x] = col_p[x] / d_t, v_t[x] = -col_a[x] / d_t of the panel's pairs (broadcast reads);
+  // u[t][x] = -d_t u_t[x], v[t][x] = d_t v_t[x] of the panel's pairs, with u_t = col_p / d_t and
+  // v_t = -col_a / d_t (broadcast reads by the later pair steps' corrections);
   // in gradient mode both are reused after the pair steps as tcol[16][kTcN], the other rows'
   // new pivot-column values sigma(x) z_j(x) read back along the pivot rows
   __align__(16) float u[8][kTcN];
@@ -44,7 +45,8 @@ struct PfTcSmem {
   float bhi[kTcN * 16], blo[kTcN * 16];  // MMA B operand
   __align__(16) float wp[16][20];        // W_P: the pivot rows' multipliers (16-byte rows)
   __align__(16) float zp[16][20];        // Z = W_P^-1, row k from pivot row k
-  uint4 pcand[4];                        // per-warp pivot candidates: key, row, -, value bits
+  uint4 pcand[4];                        // per-warp pivot candidates: key, row, position, value bits
+  float pinv[4];                         // 1 / d of each warp's candidate (0 for d = 0)
   int cand_f[4];                         // scratch (the singular flag at the end)
   int at[kTcN];                          // position -> row (virtual pivoting)
   int pidx[16];                          // the panel's pivot rows a_0, p_0, a_1, p_1, ...
@@ -118,8 +120,8 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
 #pragma unroll
             for (int t = 0; t < 8; ++t)
               if (t < s) {
-                cu = fmaf(ur[t], dr[t] * S.v[t][a], cu);
-                cv = fmaf(vr[t], -dr[t] * S.u[t][a], cv);
+                cu = fmaf(ur[t], S.v[t][a], cu);
+                cv = fmaf(vr[t], S.u[t][a], cv);
               }
             umma::tmem_wait_ld();
             colA -= cu + cv;
@@ -129,12 +131,18 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
           const unsigned key = piv_key(colA, live);
           const unsigned km = __reduce_max_sync(0xffffffffu, key);
           const int wi = __reduce_min_sync(0xffffffffu, key == km ? x : 0x7fffffff);
-          if (x == wi) S.pcand[warp] = make_uint4(km, (unsigned)wi, (unsigned)pos, __float_as_uint(colA));
+          if (x == wi) {
+            // the candidate's reciprocal pivot, once per warp (read back by every thread)
+            const float dw = -colA;
+            S.pinv[warp] = dw == 0.f ? 0.f : __fdiv_rn(1.f, dw);
+            S.pcand[warp] = make_uint4(km, (unsigned)wi, (unsigned)pos, __float_as_uint(colA));
+          }
           __syncthreads();
           uint4 hd[4];
 #pragma unroll
           for (int w = 0; w < 4; ++w) hd[w] = S.pcand[w];
           unsigned bk = hd[0].x, bp = hd[0].y, bq = hd[0].z, bvb = hd[0].w;
+          int bw = 0;
 #pragma unroll
           for (int w = 1; w < 4; ++w)
             if (hd[w].x > bk || (hd[w].x == bk && hd[w].y < bp)) {
@@ -142,10 +150,11 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
               bp = hd[w].y;
               bq = hd[w].z;
               bvb = hd[w].w;
+              bw = w;
             }
           const int p = (int)bp, q = (int)bq;  // the pivot row and its position
           const float d = -__uint_as_float(bvb);  // all candidates NaN: the first one, d = NaN
-          const float inv = d == 0.f ? 0.f : __fdiv_rn(1.f, d);
+          const float inv = S.pinv[bw];
           if (x == p) live = false;
           float colP = __uint_as_float(umma::tmem_ld1(trow + p));
           {
@@ -153,8 +162,8 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
 #pragma unroll
             for (int t = 0; t < 8; ++t)
               if (t < s) {
-                cu = fmaf(ur[t], dr[t] * S.v[t][p], cu);
-                cv = fmaf(vr[t], -dr[t] * S.u[t][p], cv);
+                cu = fmaf(ur[t], S.v[t][p], cu);
+                cv = fmaf(vr[t], S.u[t][p], cv);
               }
             umma::tmem_wait_ld();
             colP -= cu + cv;
@@ -163,8 +172,10 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
           vr[s] = -colA * inv;
           dr[s] = d;
           ir[s] = inv;
-          S.u[s][x] = ur[s];
-          S.v[s][x] = vr[s];
+          // stored pre-multiplied by the pair pivot: the products every thread formed
+          // for its corrections (d v_s and -d u_s), the same bits computed once
+          S.u[s][x] = -d * ur[s];
+          S.v[s][x] = d * vr[s];
           // the interchange of positions c + 1 and q, written by the two rows involved
           if (q != c + 1) {
             par ^= 1;
