@@ -35,18 +35,22 @@
 namespace fx {
 
 struct PfTcSmem {
-  // u[t][x] = -d_t u_t[x], v[t][x] = d_t v_t[x] of the panel's pairs, with u_t = col_p / d_t and
-  // v_t = -col_a / d_t (broadcast reads by the later pair steps' corrections);
-  // in gradient mode both are reused after the pair steps as tcol[16][kTcN], the other rows'
-  // new pivot-column values sigma(x) z_j(x) read back along the pivot rows
-  __align__(16) float u[8][kTcN];
-  float v[8][kTcN];
+  // uv[t][x] = (-d_t u_t[x], d_t v_t[x]) of the panel's pairs, with u_t = col_p / d_t and
+  // v_t = -col_a / d_t (one 8-byte broadcast read per earlier pair in the later pair steps'
+  // corrections); in gradient mode the same 8 KB are reused after the pair steps as
+  // tcol[16][kTcN], the other rows' new pivot-column values sigma(x) z_j(x) read back along
+  // the pivot rows
+  __align__(16) float2 uv[8][kTcN];
   float whi[kTcN * 16], wlo[kTcN * 16];  // MMA A operand (K-major, interleaved), TF32 hi / lo
   float bhi[kTcN * 16], blo[kTcN * 16];  // MMA B operand
   __align__(16) float wp[16][20];        // W_P: the pivot rows' multipliers (16-byte rows)
   __align__(16) float zp[16][20];        // Z = W_P^-1, row k from pivot row k
-  uint4 pcand[4];                        // per-warp pivot candidates: key, row, position, value bits
-  float pinv[4];                         // 1 / d of each warp's candidate (0 for d = 0)
+  __align__(16) float ppm[16][20];       // A'_PP = -A_PP^-1, formed by the whole block
+  // per-warp pivot candidates: packed order key (|value| key << 32 | ~row: the largest key,
+  // then the smallest row, is the largest number) and the record (position, value bits,
+  // reciprocal pivot bits) of the warp's candidate
+  __align__(16) unsigned long long pkey[4];
+  uint4 prec[4];
   int cand_f[4];                         // scratch (the singular flag at the end)
   int at[kTcN];                          // position -> row (virtual pivoting)
   int pidx[16];                          // the panel's pivot rows a_0, p_0, a_1, p_1, ...
@@ -55,7 +59,6 @@ struct PfTcSmem {
   int bad;
   uint64_t mbar;
 };
-static_assert(offsetof(PfTcSmem, v) == offsetof(PfTcSmem, u) + sizeof(float) * 8 * kTcN, "u, v contiguous");
 
 template <bool GRAD>
 __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
@@ -120,41 +123,38 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
 #pragma unroll
             for (int t = 0; t < 8; ++t)
               if (t < s) {
-                cu = fmaf(ur[t], S.v[t][a], cu);
-                cv = fmaf(vr[t], S.u[t][a], cv);
+                const float2 w = S.uv[t][a];
+                cu = fmaf(ur[t], w.y, cu);
+                cv = fmaf(vr[t], w.x, cv);
               }
             umma::tmem_wait_ld();
             colA -= cu + cv;
           }
           // pivot: largest |colA| over the unassigned rows (first occurrence): per warp two
-          // redux.sync on the packed key, then the four warps' candidates
+          // redux.sync on the packed key, then the largest of the four warps' packed keys
           const unsigned key = piv_key(colA, live);
           const unsigned km = __reduce_max_sync(0xffffffffu, key);
           const int wi = __reduce_min_sync(0xffffffffu, key == km ? x : 0x7fffffff);
           if (x == wi) {
             // the candidate's reciprocal pivot, once per warp (read back by every thread)
             const float dw = -colA;
-            S.pinv[warp] = dw == 0.f ? 0.f : __fdiv_rn(1.f, dw);
-            S.pcand[warp] = make_uint4(km, (unsigned)wi, (unsigned)pos, __float_as_uint(colA));
+            const float pinv = dw == 0.f ? 0.f : __fdiv_rn(1.f, dw);
+            S.pkey[warp] = ((unsigned long long)km << 32) | (unsigned)~wi;
+            S.prec[warp] = make_uint4((unsigned)pos, __float_as_uint(colA), __float_as_uint(pinv), 0u);
           }
           __syncthreads();
-          uint4 hd[4];
-#pragma unroll
-          for (int w = 0; w < 4; ++w) hd[w] = S.pcand[w];
-          unsigned bk = hd[0].x, bp = hd[0].y, bq = hd[0].z, bvb = hd[0].w;
-          int bw = 0;
-#pragma unroll
-          for (int w = 1; w < 4; ++w)
-            if (hd[w].x > bk || (hd[w].x == bk && hd[w].y < bp)) {
-              bk = hd[w].x;
-              bp = hd[w].y;
-              bq = hd[w].z;
-              bvb = hd[w].w;
-              bw = w;
-            }
-          const int p = (int)bp, q = (int)bq;  // the pivot row and its position
-          const float d = -__uint_as_float(bvb);  // all candidates NaN: the first one, d = NaN
-          const float inv = S.pinv[bw];
+          int p;
+          {
+            const ulonglong2 k01 = *reinterpret_cast<const ulonglong2*>(&S.pkey[0]);
+            const ulonglong2 k23 = *reinterpret_cast<const ulonglong2*>(&S.pkey[2]);
+            const unsigned long long m01 = k01.x > k01.y ? k01.x : k01.y;
+            const unsigned long long m23 = k23.x > k23.y ? k23.x : k23.y;
+            p = (int)~(unsigned)(m01 > m23 ? m01 : m23);  // the pivot row (owned by warp p / 32)
+          }
+          const uint4 rec = S.prec[p >> 5];
+          const int q = (int)rec.x;                 // the pivot row's position
+          const float d = -__uint_as_float(rec.y);  // all candidates NaN: the first one, d = NaN
+          const float inv = __uint_as_float(rec.z);
           if (x == p) live = false;
           float colP = __uint_as_float(umma::tmem_ld1(trow + p));
           {
@@ -162,8 +162,9 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
 #pragma unroll
             for (int t = 0; t < 8; ++t)
               if (t < s) {
-                cu = fmaf(ur[t], S.v[t][p], cu);
-                cv = fmaf(vr[t], S.u[t][p], cv);
+                const float2 w = S.uv[t][p];
+                cu = fmaf(ur[t], w.y, cu);
+                cv = fmaf(vr[t], w.x, cv);
               }
             umma::tmem_wait_ld();
             colP -= cu + cv;
@@ -174,8 +175,7 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
           ir[s] = inv;
           // stored pre-multiplied by the pair pivot: the products every thread formed
           // for its corrections (d v_s and -d u_s), the same bits computed once
-          S.u[s][x] = -d * ur[s];
-          S.v[s][x] = d * vr[s];
+          S.uv[s][x] = make_float2(-d * ur[s], d * vr[s]);
           // the interchange of positions c + 1 and q, written by the two rows involved
           if (q != c + 1) {
             par ^= 1;
@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
         }
         // the other rows' new pivot-column values, transposed through shared memory for the
         // pivot rows (A'_PY = sigma(y) A'_YP^T); pivot row kx keeps its row of Z
-        float* tcol = &S.u[0][0];
+        float* tcol = reinterpret_cast<float*>(&S.uv[0][0]);
         if (kx < 0) {
           const float sg = swept_before ? -1.f : 1.f;
 #pragma unroll
@@ -303,25 +303,34 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
           for (int q = 0; q < 4; ++q) z4[q] = make_float4(z[4 * q], z[4 * q + 1], z[4 * q + 2], z[4 * q + 3]);
         }
         __syncthreads();
-        // pivot row kx: A'_PP row = -(Z^T D_J^-T Z)[kx]
-        //   = sum_t (Z[2t][kx] Z[2t+1] - Z[2t+1][kx] Z[2t]) / d_t   (Z[j][kx] = 0 for j < kx)
-        if (kx >= 0) {
+        // A'_PP = -(Z^T D_J^-T Z), entry (k, j) = sum_t (Z[2t][k] Z[2t+1][j] - Z[2t+1][k] Z[2t][j]) / d_t
+        // (Z[j][k] = 0 for j < k), two entries of one row per thread
+        {
+          const int k = tid >> 3, j = 2 * (tid & 7);
+          float p0 = 0.f, p1 = 0.f;
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
-            if (t < np && 2 * t + 1 >= kx) {
+            if (t < np && 2 * t + 1 >= k) {
               const float id = ir[t];
-              const float za = S.zp[2 * t][kx] * id, zb = S.zp[2 * t + 1][kx] * id;
-              const float4* r0 = reinterpret_cast<const float4*>(S.zp[2 * t]);
-              const float4* r1 = reinterpret_cast<const float4*>(S.zp[2 * t + 1]);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float4 a = r0[q], c = r1[q];
-                pp[4 * q] = fmaf(za, c.x, fmaf(-zb, a.x, pp[4 * q]));
-                pp[4 * q + 1] = fmaf(za, c.y, fmaf(-zb, a.y, pp[4 * q + 1]));
-                pp[4 * q + 2] = fmaf(za, c.z, fmaf(-zb, a.z, pp[4 * q + 2]));
-                pp[4 * q + 3] = fmaf(za, c.w, fmaf(-zb, a.w, pp[4 * q + 3]));
-              }
+              const float za = S.zp[2 * t][k] * id, zb = S.zp[2 * t + 1][k] * id;
+              const float2 a = *reinterpret_cast<const float2*>(&S.zp[2 * t][j]);
+              const float2 c = *reinterpret_cast<const float2*>(&S.zp[2 * t + 1][j]);
+              p0 = fmaf(za, c.x, fmaf(-zb, a.x, p0));
+              p1 = fmaf(za, c.y, fmaf(-zb, a.y, p1));
             }
+          }
+          *reinterpret_cast<float2*>(&S.ppm[k][j]) = make_float2(p0, p1);
+        }
+        __syncthreads();
+        if (kx >= 0) {
+          const float4* r4 = reinterpret_cast<const float4*>(S.ppm[kx]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = r4[q];
+            pp[4 * q] = v.x;
+            pp[4 * q + 1] = v.y;
+            pp[4 * q + 2] = v.z;
+            pp[4 * q + 3] = v.w;
           }
         }
       }
@@ -341,7 +350,7 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
         // pivot rows: the whole row from the transposed values (a warp holding a pivot row
         // stores all its lanes, the other lanes write back their own row)
         if (__any_sync(0xffffffffu, kx >= 0)) {
-          const float* trow_src = &S.u[0][0] + (kx >= 0 ? kx : 0) * kTcN;
+          const float* trow_src = reinterpret_cast<const float*>(&S.uv[0][0]) + (kx >= 0 ? kx : 0) * kTcN;
 #pragma unroll 1
           for (int c0 = 0; c0 < kTcN; c0 += 32) {
             uint32_t w[32];
