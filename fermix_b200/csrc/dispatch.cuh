@@ -87,7 +87,8 @@ int launch_fused(cudaStream_t s, Job<T> J, void* ws, size_t ws_bytes);
 
 // ---- launch_tc.cu
 inline bool use_pf_tc(int dtype_is_f32, int prec, int n, int mode) {
-  return dtype_is_f32 && prec != FX_PREC_IEEE && n >= 8 && n <= kTcN && (mode == MODE_FWD || mode == MODE_SLOG_GRAD);
+  (void)prec;  // tf32x3 and ieee both (tensor-core or FMA block updates)
+  return dtype_is_f32 && n >= 8 && n <= kTcN && (mode == MODE_FWD || mode == MODE_SLOG_GRAD);
 }
 inline bool use_lu_tc(int dtype_is_f32, int prec, int n, int mode) {
   return dtype_is_f32 && prec != FX_PREC_IEEE && n >= 8 && n <= 2 * kTcN &&

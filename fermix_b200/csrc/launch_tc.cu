@@ -1,22 +1,25 @@
-// Tensor-memory (tcgen05) kernels: float32, prec tf32x3, slogpf n <= 128 and slogdet
-// n <= 256, forward and slogdet / slogpf gradient.
+// Tensor-memory (tcgen05) kernels: float32, slogpf n <= 128 (prec tf32x3 and ieee) and
+// slogdet n <= 256 (prec tf32x3), forward and slogdet / slogpf gradient.
 #include "dispatch.cuh"
 #include "lu_tc.cuh"
 #include "pf_tc.cuh"
 
 namespace fxh {
 
-// Tensor-core slogpf (float32, prec tf32x3, 8 <= n <= 128, forward or slogpf gradient):
-// one 128-thread block per matrix, the matrix resident in TMEM (128 of the SM's 512
-// columns). The shared-memory request is padded so that exactly four blocks share an SM
-// (four blocks use all 512 TMEM columns; a fifth would wait in tcgen05.alloc).
+// Tensor-memory slogpf (float32, 8 <= n <= 128, forward or slogpf gradient): one 128-thread
+// block per matrix, the matrix resident in TMEM (128 of the SM's 512 columns); the block
+// updates run on the tensor cores under tf32x3 and as IEEE FMAs under prec ieee. The
+// shared-memory request is padded so that exactly four blocks share an SM (four blocks use
+// all 512 TMEM columns; a fifth would wait in tcgen05.alloc).
 constexpr size_t kTcSmem = 50 * 1024;
 static_assert(sizeof(PfTcSmem) <= kTcSmem, "PfTcSmem too large");
 
 int launch_pf_tc(cudaStream_t s, Job<float> J) {
   const DevInfo* D = dev_info();
   if (!D) return FX_ERR_DEVICE;
-  void* k = J.mode == MODE_FWD ? (void*)&pf_tc_kernel<false> : (void*)&pf_tc_kernel<true>;
+  const bool ieee = J.prec == FX_PREC_IEEE;
+  void* k = J.mode == MODE_FWD ? (ieee ? (void*)&pf_tc_kernel<false, true> : (void*)&pf_tc_kernel<false, false>)
+                               : (ieee ? (void*)&pf_tc_kernel<true, true> : (void*)&pf_tc_kernel<true, false>);
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem) != cudaSuccess)
     return FX_ERR_CUDA;
   if (cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)

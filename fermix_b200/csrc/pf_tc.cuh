@@ -51,6 +51,7 @@ struct PfTcSmem {
   // reciprocal pivot bits) of the warp's candidate
   __align__(16) unsigned long long pkey[4];
   uint4 prec[4];
+  unsigned cmask[4];                     // prec ieee forward: the unswept rows (columns to update)
   int cand_f[4];                         // scratch (the singular flag at the end)
   int at[kTcN];                          // position -> row (virtual pivoting)
   int pidx[16];                          // the panel's pivot rows a_0, p_0, a_1, p_1, ...
@@ -60,7 +61,70 @@ struct PfTcSmem {
   uint64_t mbar;
 };
 
+static_assert(sizeof(PfTcSmem::uv) == sizeof(float) * 16 * kTcN, "uv holds tcol[16][kTcN]");
+
+// prec ieee: B's rows (16 values, 80-byte rows: conflict-free 16-byte stores) in the space
+// of the tensor-core operands whi / wlo, which that mode does not use
+__device__ __forceinline__ float (*pf_tc_brow(PfTcSmem& S))[20] { return reinterpret_cast<float (*)[20]>(S.whi); }
+static_assert(offsetof(PfTcSmem, wlo) == offsetof(PfTcSmem, whi) + sizeof(float) * kTcN * 16 &&
+                  sizeof(float) * kTcN * 20 <= 2 * sizeof(float) * kTcN * 16,
+              "brow fits whi + wlo");
+
+// prec ieee: the rank-16 update D -= W B^T of this thread's TMEM row with IEEE float32 FMAs
+// (one sequential chain per entry over the panel's pairs, u then v of each pair), W = this
+// row's (u_t, v_t), B's rows broadcast from shared memory; 16 columns per TMEM round trip.
+// The forward updates only its unswept rows and columns (the rest is never read again).
 template <bool GRAD>
+__device__ __forceinline__ void pf_tc_fma_update(PfTcSmem& S, uint32_t trow, int n, int np, const float (&ur)[8],
+                                                 const float (&vr)[8], bool live) {
+  if (!GRAD && !__any_sync(0xffffffffu, live)) return;
+  const float(*brow)[20] = pf_tc_brow(S);
+#pragma unroll 1
+  for (int c0 = 0; c0 < n; c0 += 16) {
+    const unsigned cm = GRAD ? 0xffffu : (S.cmask[c0 >> 5] >> (c0 & 16)) & 0xffffu;
+    if (cm == 0u) continue;
+    uint32_t w0[8], w1[8];
+    umma::tmem_ld8(trow + c0, w0);
+    umma::tmem_ld8(trow + c0 + 8, w1);
+    umma::tmem_wait_ld();
+    float v[16];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      v[e] = __uint_as_float(w0[e]);
+      v[e + 8] = __uint_as_float(w1[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      if ((cm >> e) & 1u) {
+        const float4* b4 = reinterpret_cast<const float4*>(brow[c0 + e]);
+        float acc = v[e];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 b = b4[q];
+          if (2 * q < np) {
+            acc = fmaf(-ur[2 * q], b.x, acc);
+            acc = fmaf(-vr[2 * q], b.y, acc);
+          }
+          if (2 * q + 1 < np) {
+            acc = fmaf(-ur[2 * q + 1], b.z, acc);
+            acc = fmaf(-vr[2 * q + 1], b.w, acc);
+          }
+        }
+        v[e] = acc;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      w0[e] = __float_as_uint(v[e]);
+      w1[e] = __float_as_uint(v[e + 8]);
+    }
+    umma::tmem_st8(trow + c0, w0);
+    umma::tmem_st8(trow + c0 + 8, w1);
+  }
+  umma::tmem_wait_st();
+}
+
+template <bool GRAD, bool IEEE>
 __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PfTcSmem& S = *reinterpret_cast<PfTcSmem*>(smem_raw);
@@ -218,8 +282,31 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
           }
         }
       }
-      // ---- MMA operands: W[x] = (u_t, v_t), B[x] = sigma(x) d_t (v_t, -u_t), 16-byte stores
-      {
+      // the forward needs no update after the last panel
+      const bool need_upd = GRAD || g0 + 8 < npairs;
+      if (IEEE) {
+        // ---- prec ieee: row y of B = sigma(y) d_t (v_t, -u_t) into brow[y] for the FMA
+        // update below; the forward only updates the columns of the unswept rows
+        if (need_upd) {
+          const float sig = swept_before ? -1.f : 1.f;
+          float4* b4 = reinterpret_cast<float4*>(pf_tc_brow(S)[x]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float e[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int k = 4 * q + c, t = k >> 1;
+              e[c] = t < np ? ((k & 1) ? -sig * dr[t] * ur[t] : sig * dr[t] * vr[t]) : 0.f;
+            }
+            b4[q] = make_float4(e[0], e[1], e[2], e[3]);
+          }
+          if (!GRAD) {
+            const unsigned lm = __ballot_sync(0xffffffffu, live);
+            if (lane == 0) S.cmask[warp] = lm;
+          }
+        }
+      } else if (need_upd) {
+        // ---- MMA operands: W[x] = (u_t, v_t), B[x] = sigma(x) d_t (v_t, -u_t), 16-byte stores
         const float sig = swept_before ? -1.f : 1.f;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -243,11 +330,11 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
           *reinterpret_cast<float4*>(&S.bhi[off]) = make_float4(zh[0], zh[1], zh[2], zh[3]);
           *reinterpret_cast<float4*>(&S.blo[off]) = make_float4(zl[0], zl[1], zl[2], zl[3]);
         }
+        umma::fence_proxy_async_smem();
       }
-      umma::fence_proxy_async_smem();
       tc_sync();
       FX_TOC(tq, 10);
-      if (tid == 0) {
+      if (!IEEE && need_upd && tid == 0) {
         const uint32_t idesc = umma::idesc_tf32(kTcN, kTcN, true);  // D -= W B^T
 #pragma unroll
         for (int sl = 0; sl < 2; ++sl) {
@@ -261,15 +348,17 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
         }
         umma::mma_commit(&S.mbar);
       }
+      // prec ieee: the FMA update now (the gradient's replacement values below only read
+      // shared memory and this thread's registers)
+      if (IEEE && need_upd) pf_tc_fma_update<GRAD>(S, trow, n, np, ur, vr, live);
       // gradient mode, while the tensor core runs the update: z W_P = rhs (rhs = this row's
       // W, or e_kx on pivot row kx), from the last row of W_P up
-      float z[16], pp[16];
+      float z[16];
       if (GRAD) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const float wj = (j & 1) ? vr[j >> 1] : ur[j >> 1];
           z[j] = kx >= 0 ? (j == kx ? 1.f : 0.f) : (j < 2 * np ? wj : 0.f);
-          pp[j] = 0.f;
         }
 #pragma unroll
         for (int m = 15; m >= 2; --m) {
@@ -323,27 +412,30 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
         }
         __syncthreads();
         if (kx >= 0) {
+          // a pivot row's new pivot-column values are its row of A'_PP (z is no longer needed)
           const float4* r4 = reinterpret_cast<const float4*>(S.ppm[kx]);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float4 v = r4[q];
-            pp[4 * q] = v.x;
-            pp[4 * q + 1] = v.y;
-            pp[4 * q + 2] = v.z;
-            pp[4 * q + 3] = v.w;
+            z[4 * q] = v.x;
+            z[4 * q + 1] = v.y;
+            z[4 * q + 2] = v.z;
+            z[4 * q + 3] = v.w;
           }
         }
       }
-      __syncwarp();
-      if (!umma::mbar_wait(&S.mbar, phase, J.wait_polls)) {
-        // give up on this member (NaN outputs, the status word records the timeout), but
-        // wait once more, with the default limit, so that no MMA is still in flight when
-        // the threads touch its operands, TMEM or the tensor memory allocation again
-        S.bad = 1;
-        (void)umma::mbar_wait(&S.mbar, phase, kTcWaitIters);
+      if (!IEEE && need_upd) {
+        __syncwarp();
+        if (!umma::mbar_wait(&S.mbar, phase, J.wait_polls)) {
+          // give up on this member (NaN outputs, the status word records the timeout), but
+          // wait once more, with the default limit, so that no MMA is still in flight when
+          // the threads touch its operands, TMEM or the tensor memory allocation again
+          S.bad = 1;
+          (void)umma::mbar_wait(&S.mbar, phase, kTcWaitIters);
+        }
+        phase ^= 1;
+        umma::fence_after_sync();
       }
-      phase ^= 1;
-      umma::fence_after_sync();
       FX_TOC(tq, 11);
 
       if (GRAD) {
@@ -387,7 +479,7 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
         // pivot columns of every row: A'_XP = z, on the pivot rows A'_PP = -A_PP^-1
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (j < 2 * np) umma::tmem_st1(trow + S.pidx[j], __float_as_uint(kx >= 0 ? pp[j] : z[j]));
+          if (j < 2 * np) umma::tmem_st1(trow + S.pidx[j], __float_as_uint(z[j]));
         umma::tmem_wait_st();
         tc_sync();
         FX_TOC(tq, 4);
