@@ -43,10 +43,15 @@ struct LuTcSmemT {
   static constexpr int NW = NR / 32;
   float chi[NR * 16], clo[NR * 16];                 // A operand C, K-major, TF32 hi / lo
   float bhi[NR * 16], bmid[NR * 16], blo[NR * 16];  // B operand, K-major, exact 3-way split
-  uint4 chead[2][NW];                               // per-warp pivot candidates by step parity: key, row, live
-  float crow[2][NW][16];                            // the candidates' current panel entries
+  // per-warp pivot candidates by step parity: packed order key (|value| key << 32 | ~row:
+  // the largest key, then the smallest row, is the largest number), the warp's unpivoted
+  // rows (ballot), the reciprocal of the candidate's pivot value and its panel entries
+  __align__(16) unsigned long long ckey[2][NW];
+  unsigned clm[2][NW];
+  float cinv[2][NW];
+  __align__(16) float crow[2][NW][16];
   float prow[16][NR + 4];                           // the panel's pivot rows (16-byte rows, conflict-free columns)
-  float L11[16][17];                                // multipliers of the pivot rows (strict lower part)
+  __align__(16) float L11[16][20];                  // multipliers of the pivot rows (strict lower part, 16-byte rows)
   float U11[16][17];                                // the pivot rows' panel entries (upper part)
   float Linv[16][17];                               // L11^-1 (gradient mode)
   float Uinv[16][17];                               // U11^-1 (gradient mode)
@@ -136,25 +141,28 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
           const unsigned lm = __ballot_sync(0xffffffffu, live);
           if (x == wi) {
             // this warp's candidate (key 0: the warp has no unpivoted row left)
-            S.chead[s & 1][warp] = make_uint4(km, (unsigned)wi, lm, 0u);
+            S.ckey[s & 1][warp] = ((unsigned long long)km << 32) | (unsigned)~wi;
+            S.clm[s & 1][warp] = lm;
+            S.cinv[s & 1][warp] = v == 0.f ? 0.f : __frcp_rn(v);
             float4* r4 = reinterpret_cast<float4*>(S.crow[s & 1][warp]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) r4[q] = make_float4(pr[4 * q], pr[4 * q + 1], pr[4 * q + 2], pr[4 * q + 3]);
           }
           __syncthreads();
-          uint4 hd[NW];
+          unsigned long long best;
+          {
+            const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(S.ckey[s & 1]);
+            const ulonglong2 k01 = k2[0];
+            best = k01.x > k01.y ? k01.x : k01.y;
 #pragma unroll
-          for (int w = 0; w < NW; ++w) hd[w] = S.chead[s & 1][w];
-          int pw = 0;
-          unsigned bk = hd[0].x, bp = hd[0].y;
-#pragma unroll
-          for (int w = 1; w < NW; ++w)
-            if (hd[w].x > bk || (hd[w].x == bk && hd[w].y < bp)) {
-              pw = w;
-              bk = hd[w].x;
-              bp = hd[w].y;
+            for (int w = 1; w < NW / 2; ++w) {
+              const ulonglong2 kw2 = k2[w];
+              const unsigned long long m = kw2.x > kw2.y ? kw2.x : kw2.y;
+              best = m > best ? m : best;
             }
-          const int p = (int)bp;
+          }
+          const int p = (int)~(unsigned)best;  // the pivot row, owned by warp p / 32
+          const int pw = p >> 5;
           float ur[16];
           {
             const float4* r4 = reinterpret_cast<const float4*>(S.crow[s & 1][pw]);
@@ -168,22 +176,24 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
             }
           }
           const float piv = ur[s];
+          const float inv = S.cinv[s & 1][pw];
           if (x == p) {
             mypos = k0 + s;
             // rows of smaller index still unpivoted: the inversions this pivot adds
-            int cnt = 0;
+            int cnt = __popc(S.clm[s & 1][warp] & ((1u << lane) - 1u));
 #pragma unroll
-            for (int w = 0; w < NW; ++w) {
-              if (w < warp) cnt += __popc(hd[w].z);
-              if (w == warp) cnt += __popc(hd[w].z & ((1u << lane) - 1u));
-            }
+            for (int w = 0; w < NW; ++w)
+              if (w < warp) cnt += __popc(S.clm[s & 1][w]);
             myinv ^= cnt & 1;
             S.dvec[k0 + s] = piv;
             S.at[k0 + s] = x;
           } else if (x < n && (GRAD ? mypos < k0 : mypos < 0)) {
             // rows outside this panel's pivots eliminate (gradient mode: rows pivoted in
-            // earlier panels too, for their multipliers)
-            const float l = piv == 0.f ? 0.f : __fdiv_rn(v, piv);
+            // earlier panels too, for their multipliers); the multiplier is v times the
+            // guarded reciprocal pivot as in the reference (src/fermix/_lu.py:170-173),
+            // exactly +-1 for a row equal to +-(the pivot row's entry), so that duplicated
+            // rows cancel to exact zeros
+            const float l = piv == 0.f ? 0.f : (v == piv ? 1.f : (v == -piv ? -1.f : v * inv));
             lr[s] = l;
 #pragma unroll
             for (int t = 0; t < 16; ++t)
@@ -193,12 +203,18 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
       }
       const bool inP = mypos >= k0 && mypos < k0 + kw;
       if (inP) {
-        // a pivot row keeps its multipliers (L11 row) and its remaining entries (U11 row)
+        // a pivot row keeps its multipliers (L11 row, zero from the diagonal on) and its
+        // remaining entries (U11 row)
         const int j = mypos - k0;
+        float4* l4 = reinterpret_cast<float4*>(S.L11[j]);
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          if (t < j) S.L11[j][t] = lr[t];
-          else if (GRAD) S.U11[j][t] = pr[t];
+        for (int q = 0; q < 4; ++q)
+          l4[q] = make_float4(4 * q < j ? lr[4 * q] : 0.f, 4 * q + 1 < j ? lr[4 * q + 1] : 0.f,
+                              4 * q + 2 < j ? lr[4 * q + 2] : 0.f, 4 * q + 3 < j ? lr[4 * q + 3] : 0.f);
+        if (GRAD) {
+#pragma unroll
+          for (int t = 0; t < 16; ++t)
+            if (t >= j) S.U11[j][t] = pr[t];
         }
       }
       __syncthreads();  // L11 / U11 / at complete
@@ -261,13 +277,27 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
 #pragma unroll
       for (int t = 0; t < 16; ++t) c[t] = 0.f;
       if (x < n && !inP && (GRAD || mypos < 0)) {
+        // c = l L11^-1 column by column from the last: c[r] is final once the rows below
+        // it are applied, then it is removed from the earlier entries with L11's row r
+        // (16-byte broadcast reads)
 #pragma unroll
-        for (int t = 15; t >= 0; --t) {
-          float acc = lr[t];
+        for (int t = 0; t < 16; ++t) c[t] = t < kw ? lr[t] : 0.f;
 #pragma unroll
-          for (int r = 0; r < 16; ++r)
-            if (r > t && r < kw) acc = fmaf(-c[r], S.L11[r][t], acc);
-          c[t] = t < kw ? acc : 0.f;
+        for (int r = 15; r >= 1; --r) {
+          if (r < kw) {
+            const float cr = c[r];
+            const float4* l4 = reinterpret_cast<const float4*>(S.L11[r]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (4 * q < r) {
+                const float4 L = l4[q];
+                const float lv[4] = {L.x, L.y, L.z, L.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  if (4 * q + e < r) c[4 * q + e] = fmaf(-cr, lv[e], c[4 * q + e]);
+              }
+            }
+          }
         }
       }
       FX_TOC(tq, 2);
