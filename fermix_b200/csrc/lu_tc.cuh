@@ -44,11 +44,11 @@ struct LuTcSmemT {
   float chi[NR * 16], clo[NR * 16];                 // A operand C, K-major, TF32 hi / lo
   float bhi[NR * 16], bmid[NR * 16], blo[NR * 16];  // B operand, K-major, exact 3-way split
   // per-warp pivot candidates by step parity: packed order key (|value| key << 32 | ~row:
-  // the largest key, then the smallest row, is the largest number), the warp's unpivoted
-  // rows (ballot), the reciprocal of the candidate's pivot value and its panel entries
+  // the largest key, then the smallest row, is the largest number), the reciprocal of the
+  // candidate's pivot value and its panel entries
   __align__(16) unsigned long long ckey[2][NW];
-  unsigned clm[2][NW];
   float cinv[2][NW];
+  unsigned clm[16][NW];  // the warps' unpivoted rows at each pivot step of the panel
   __align__(16) float crow[2][NW][16];
   float prow[16][NR + 4];                           // the panel's pivot rows (16-byte rows, conflict-free columns)
   __align__(16) float L11[16][20];                  // multipliers of the pivot rows (strict lower part, 16-byte rows)
@@ -136,14 +136,17 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
           const bool live = mypos < 0;
           const float v = pr[s];
           const unsigned key = piv_key(v, live);
+          // every lane forms its reciprocal while the reductions run (only the winner's is kept)
+          const float vinv = v == 0.f ? 0.f : __frcp_rn(v);
           const unsigned km = __reduce_max_sync(0xffffffffu, key);
-          const int wi = __reduce_min_sync(0xffffffffu, key == km ? x : 0x7fffffff);
+          // the first lane holding the largest key: the smallest row
+          const int wi = (warp << 5) + __ffs(__ballot_sync(0xffffffffu, key == km)) - 1;
           const unsigned lm = __ballot_sync(0xffffffffu, live);
           if (x == wi) {
             // this warp's candidate (key 0: the warp has no unpivoted row left)
             S.ckey[s & 1][warp] = ((unsigned long long)km << 32) | (unsigned)~wi;
-            S.clm[s & 1][warp] = lm;
-            S.cinv[s & 1][warp] = v == 0.f ? 0.f : __frcp_rn(v);
+            S.clm[s][warp] = lm;
+            S.cinv[s & 1][warp] = vinv;
             float4* r4 = reinterpret_cast<float4*>(S.crow[s & 1][warp]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) r4[q] = make_float4(pr[4 * q], pr[4 * q + 1], pr[4 * q + 2], pr[4 * q + 3]);
@@ -179,12 +182,6 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
           const float inv = S.cinv[s & 1][pw];
           if (x == p) {
             mypos = k0 + s;
-            // rows of smaller index still unpivoted: the inversions this pivot adds
-            int cnt = __popc(S.clm[s & 1][warp] & ((1u << lane) - 1u));
-#pragma unroll
-            for (int w = 0; w < NW; ++w)
-              if (w < warp) cnt += __popc(S.clm[s & 1][w]);
-            myinv ^= cnt & 1;
             S.dvec[k0 + s] = piv;
             S.at[k0 + s] = x;
           } else if (x < n && (GRAD ? mypos < k0 : mypos < 0)) {
@@ -204,8 +201,14 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
       const bool inP = mypos >= k0 && mypos < k0 + kw;
       if (inP) {
         // a pivot row keeps its multipliers (L11 row, zero from the diagonal on) and its
-        // remaining entries (U11 row)
+        // remaining entries (U11 row), and counts the inversions it added: the rows of
+        // smaller index still unpivoted at its step (the warps' ballots recorded then)
         const int j = mypos - k0;
+        int cnt = __popc(S.clm[j][warp] & ((1u << lane) - 1u));
+#pragma unroll
+        for (int w = 0; w < NW; ++w)
+          if (w < warp) cnt += __popc(S.clm[j][w]);
+        myinv = cnt & 1;
         float4* l4 = reinterpret_cast<float4*>(S.L11[j]);
 #pragma unroll
         for (int q = 0; q < 4; ++q)

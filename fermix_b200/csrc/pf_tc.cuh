@@ -59,6 +59,7 @@ struct PfTcSmem {
   uint32_t tslot;
   int bad;
   uint64_t mbar;
+  uint64_t lbar[2];  // the staged load's two chunk buffers
 };
 
 static_assert(sizeof(PfTcSmem::uv) == sizeof(float) * 16 * kTcN, "uv holds tcol[16][kTcN]");
@@ -124,6 +125,121 @@ __device__ __forceinline__ void pf_tc_fma_update(PfTcSmem& S, uint32_t trow, int
   umma::tmem_wait_st();
 }
 
+// skew_symmetrize load through shared memory: 32-row chunks of A (528-byte rows, one bulk copy
+// per row) in two buffers over the space of uv and the tensor-core operands (free between
+// matrices). TMEM starts at zero; chunk c adds -A[32c + k][x] / 2 to every row's column block
+// c (conflict-free column reads) and, on warp c, A[x][y] / 2 to its own rows (16-byte reads),
+// so every entry is round(A[x][y] / 2 - A[y][x] / 2), the bits of (A[x][y] - A[y][x]) / 2.
+// Needs n % 4 == 0 and a 16-byte aligned matrix (the rows are bulk copies).
+constexpr int kTcStgLd = 132;  // staged row stride (floats): 16-byte rows, bank offset 4 per row
+__device__ __forceinline__ float (*pf_tc_stage(PfTcSmem& S, int buf))[kTcStgLd] {
+  return reinterpret_cast<float (*)[kTcStgLd]>(reinterpret_cast<unsigned char*>(&S.uv[0][0]) +
+                                                (size_t)buf * 32 * kTcStgLd * sizeof(float));
+}
+static_assert(offsetof(PfTcSmem, whi) == sizeof(PfTcSmem::uv) && offsetof(PfTcSmem, blo) + sizeof(PfTcSmem::blo) ==
+                  sizeof(PfTcSmem::uv) + 4 * sizeof(PfTcSmem::whi) &&
+                  2 * 32 * kTcStgLd * sizeof(float) <= sizeof(PfTcSmem::uv) + 4 * sizeof(PfTcSmem::whi),
+              "the staging buffers fit uv and the operands");
+
+// warp 0: rows 32 c .. of the matrix into buffer c & 1 (lane l copies row 32 c + l)
+__device__ __forceinline__ void pf_tc_stage_issue(PfTcSmem& S, const float* src, int n, int c, int lane) {
+  const int rows = min(32, n - 32 * c);
+  uint64_t* bar = &S.lbar[c & 1];
+  umma::fence_proxy_async_smem();  // the buffer's earlier generic accesses before the copies
+  if (lane == 0) umma::mbar_arrive_expect_tx(bar, (uint32_t)(rows * n * 4));
+  __syncwarp();
+  if (lane < rows) umma::bulk_g2s(pf_tc_stage(S, c & 1)[lane], src + (size_t)(32 * c + lane) * n, (uint32_t)n * 4u, bar);
+}
+
+// returns false when a chunk wait ran out (the member is then marked bad by the caller)
+__device__ __forceinline__ bool pf_tc_load_skew_staged(PfTcSmem& S, const float* src, int n, uint32_t trow, int x,
+                                                       int warp, int lane, uint32_t& lph, uint32_t polls) {
+  const int nc = (n + 31) >> 5;
+  if (warp == 0) {
+    pf_tc_stage_issue(S, src, n, 0, lane);
+    if (nc > 1) pf_tc_stage_issue(S, src, n, 1, lane);
+  }
+  {
+    uint32_t z[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int c = 0; c < kTcN; c += 8) umma::tmem_st8(trow + c, z);
+    umma::tmem_wait_st();
+  }
+  bool ok = true;
+#pragma unroll 1
+  for (int c = 0; c < nc; ++c) {
+    const int bufi = c & 1;
+    const uint32_t par = (lph >> bufi) & 1u;
+    if (!umma::mbar_wait(&S.lbar[bufi], par, polls)) {
+      ok = false;
+      (void)umma::mbar_wait(&S.lbar[bufi], par, kTcWaitIters);  // no copy left in flight
+    }
+    lph ^= 1u << bufi;
+    const float(*buf)[kTcStgLd] = pf_tc_stage(S, bufi);
+    // every row: column block c -= A[32 c + k][x] / 2
+    {
+      uint32_t w[32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t t8[8];
+        umma::tmem_ld8(trow + 32 * c + 8 * q, t8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[8 * q + e] = t8[e];
+      }
+      umma::tmem_wait_ld();
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const float cv = (x < n && 32 * c + k < n) ? buf[k][x] : 0.f;
+        w[k] = __float_as_uint(fmaf(-0.5f, cv, __uint_as_float(w[k])));
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t t8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t8[e] = w[8 * q + e];
+        umma::tmem_st8(trow + 32 * c + 8 * q, t8);
+      }
+      umma::tmem_wait_st();
+    }
+    // warp c's own rows: += A[x][y] / 2
+    if (warp == c) {
+      const float* row = buf[x - 32 * c];
+#pragma unroll 1
+      for (int cb = 0; cb < kTcN; cb += 32) {
+        uint32_t w[32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t t8[8];
+          umma::tmem_ld8(trow + cb + 8 * q, t8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) w[8 * q + e] = t8[e];
+        }
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const bool in = x < n && cb + 4 * q < n;  // n % 4 == 0: whole 16-byte pieces
+          const float4 r = in ? *reinterpret_cast<const float4*>(row + cb + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+          w[4 * q] = __float_as_uint(fmaf(0.5f, r.x, __uint_as_float(w[4 * q])));
+          w[4 * q + 1] = __float_as_uint(fmaf(0.5f, r.y, __uint_as_float(w[4 * q + 1])));
+          w[4 * q + 2] = __float_as_uint(fmaf(0.5f, r.z, __uint_as_float(w[4 * q + 2])));
+          w[4 * q + 3] = __float_as_uint(fmaf(0.5f, r.w, __uint_as_float(w[4 * q + 3])));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t t8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t8[e] = w[8 * q + e];
+          umma::tmem_st8(trow + cb + 8 * q, t8);
+        }
+      }
+      umma::tmem_wait_st();
+    }
+    __syncthreads();  // every thread is done with this buffer
+    if (c + 2 < nc && warp == 0) pf_tc_stage_issue(S, src, n, c + 2, lane);
+  }
+  return ok;
+}
+
 template <bool GRAD, bool IEEE>
 __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -137,6 +253,8 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
   }
   if (tid == 0) {
     umma::mbar_init(&S.mbar, 1);
+    umma::mbar_init(&S.lbar[0], 1);
+    umma::mbar_init(&S.lbar[1], 1);
     umma::fence_mbar_init();
   }
   tc_sync();
@@ -146,6 +264,9 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
   const uint32_t tbase = S.tslot;
   const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);
   uint32_t phase = 0;
+  uint32_t lph = 0u;  // the staged load's buffer phases (bit i: buffer i)
+  // skew_symmetrize through the staged load when every row is a whole number of 16-byte pieces
+  const bool staged = J.skew != 0 && (n & 3) == 0 && (reinterpret_cast<uintptr_t>(J.a) & 15) == 0;
 
   for (int64_t b = blockIdx.x; b < J.B; b += gridDim.x) {
     FX_TIC(tq);
@@ -153,9 +274,14 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
     // next matrix starts streaming into L2 meanwhile
     const float* src = J.a + b * (int64_t)n * n;
     if (tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
-    tc_load_matrix(src, n, J.skew != 0, trow, x);
-    S.at[x] = x;
     if (tid == 0) S.bad = 0;
+    if (staged) {
+      __syncthreads();  // S.bad cleared before a chunk wait can set it
+      if (!pf_tc_load_skew_staged(S, src, n, trow, x, warp, lane, lph, J.wait_polls) && lane == 0) S.bad = 1;
+    } else {
+      tc_load_matrix(src, n, J.skew != 0, trow, x);
+    }
+    S.at[x] = x;
     // virtual pivoting: each thread tracks its own row's position; every thread keeps the
     // interchange parity (all see the same pivots)
     int pos = x, par = 0;
@@ -197,12 +323,13 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
           // pivot: largest |colA| over the unassigned rows (first occurrence): per warp two
           // redux.sync on the packed key, then the largest of the four warps' packed keys
           const unsigned key = piv_key(colA, live);
+          // every lane forms its reciprocal pivot 1 / (-colA) while the reductions run (only
+          // the warp's candidate keeps it)
+          const float pinv = colA == 0.f ? 0.f : __frcp_rn(-colA);
           const unsigned km = __reduce_max_sync(0xffffffffu, key);
-          const int wi = __reduce_min_sync(0xffffffffu, key == km ? x : 0x7fffffff);
+          // the first lane holding the largest key: the smallest row
+          const int wi = (warp << 5) + __ffs(__ballot_sync(0xffffffffu, key == km)) - 1;
           if (x == wi) {
-            // the candidate's reciprocal pivot, once per warp (read back by every thread)
-            const float dw = -colA;
-            const float pinv = dw == 0.f ? 0.f : __fdiv_rn(1.f, dw);
             S.pkey[warp] = ((unsigned long long)km << 32) | (unsigned)~wi;
             S.prec[warp] = make_uint4((unsigned)pos, __float_as_uint(colA), __float_as_uint(pinv), 0u);
           }
