@@ -608,10 +608,11 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
         for (int j = 0; j < 16; ++j)
           if (j < 2 * np) umma::tmem_st1(trow + S.pidx[j], __float_as_uint(z[j]));
         umma::tmem_wait_st();
-        tc_sync();
         FX_TOC(tq, 4);
       }
-      __syncthreads();
+      // the panel's pidx / at / dvec are read before the next panel's pair steps rewrite them;
+      // TMEM stores complete before the next MMA (or the final read) on any thread
+      tc_sync();
       FX_TOC(tq, 12);
     }
 
