@@ -334,11 +334,15 @@ __global__ void __launch_bounds__(128, 2) lg_tc_update_kernel(LgArgs<T> A, int r
 // ---------------------------------------------------------------- float64 / complex128
 // The same trailing update on the FP64 tensor cores (DMMA, mma.sync m8n8k4 f64) for the
 // 64-bit dtypes, whose prec is always "ieee": every product and sum is an IEEE fp64
-// fused multiply-add, as in the FMA kernel. A 256-thread CTA owns a 128-row x 64-column
-// tile (complex128: 32 complex columns); its 8 warps (4 x 2) own 32 x 32 sub-tiles (complex:
-// 32 x 16, real and imaginary accumulators). The accumulators start as the M tile and the
-// coefficients are staged negated, so D = M + (-C) P is the update itself; a row
-// duplicating pivot row s (coefficients e_s) ends as fma(-1, P_s, M) = 0 exactly.
+// fused multiply-add, as in the FMA kernel. A 256-thread CTA owns a 128-row strip and walks
+// a run of kLgDmTiles column tiles of 64 columns (complex128: 32 complex columns) in it; its
+// 8 warps (4 x 2) own 32 x 32 sub-tiles (complex: 32 x 16, real and imaginary
+// accumulators). -C is staged in shared memory once per CTA; while one tile's products and
+// stores run, the next tile's M entries (into a second register set) and P rows are already
+// in flight, so the loads that bound a one-tile CTA overlap the rest. The accumulators start
+// as the M tile and the coefficients are staged negated, so D = M + (-C) P is the update
+// itself; a row duplicating pivot row s (coefficients e_s) ends as fma(-1, P_s, M) = 0
+// exactly.
 //
 // m8n8k4 fragments (lane = 4 g + t): A element (g, t), B element (t, g), accumulator
 // elements (g, 2 t) and (g, 2 t + 1). Shared-memory row strides are 4 (mod 16) doubles, so
@@ -348,6 +352,8 @@ __device__ __forceinline__ void dmma(double& d0, double& d1, double a, double b)
                : "+d"(d0), "+d"(d1)
                : "d"(a), "d"(b));
 }
+
+constexpr int kLgDmTiles = 4;  // column tiles per CTA
 
 template <typename T>
 struct LgDm;
@@ -375,26 +381,10 @@ constexpr size_t lg_dm_smem() {
   return sizeof(LgDmSmem<T>);
 }
 
-template <typename T, bool SKEW>
-__global__ void __launch_bounds__(256, 2) lg_dmma_update_kernel(LgArgs<T> A, int r_lo, int c_lo) {
-  constexpr bool CX = Sc<T>::cx;
-  constexpr int NB = LgDm<T>::NB, TC = LgDm<T>::TC, WC = LgDm<T>::WC;
-  constexpr int SA = LgDmSmem<T>::SA, SB = LgDmSmem<T>::SB;
-  constexpr int MT = 4, NT = WC / 8;  // 8 x 8 accumulator tiles of a warp
-  extern __shared__ __align__(16) unsigned char lgdm_raw[];
-  LgDmSmem<T>& S = *reinterpret_cast<LgDmSmem<T>*>(lgdm_raw);
-  const int b = blockIdx.z, n = A.n, k0 = A.k0, kw = A.kw;
-  const int r0 = r_lo + blockIdx.y * 128, c0 = c_lo + blockIdx.x * TC;
-  if (SKEW && c0 >= r0 + 128) return;  // tile entirely above the diagonal
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int wr = r0 + (warp >> 1) * 32, wc = c0 + (warp & 1) * WC;  // this warp's sub-tile
-  T* Mb = A.M + (size_t)b * n * n;
-  const T* Cb = A.C + (size_t)b * n * NB;
-  const T* Pb = A.P + (size_t)b * NB * n;
-
-  // ---- accumulators = the M tile (re / im)
-  double dr[MT][NT][2], di[CX ? MT : 1][CX ? NT : 1][2];
+// The warp's M sub-tile at column offset c0 (zero outside n x n) into accumulator layout.
+template <typename T, int MT, int NT>
+__device__ __forceinline__ void lg_dm_load_m(const T* __restrict__ Mb, int n, int wr, int wc, int g, int t,
+                                             double (&vr)[MT][NT][2], double (&vi)[Sc<T>::cx ? MT : 1][Sc<T>::cx ? NT : 1][2]) {
 #pragma unroll
   for (int i = 0; i < MT; ++i)
 #pragma unroll
@@ -403,14 +393,42 @@ __global__ void __launch_bounds__(256, 2) lg_dmma_update_kernel(LgArgs<T> A, int
       for (int e = 0; e < 2; ++e) {
         const int rr = wr + 8 * i + g, cc = wc + 8 * j + 2 * t + e;
         const T v = (rr < n && cc < n) ? Mb[(size_t)rr * n + cc] : s_zero<T>();
-        if constexpr (CX) {
-          dr[i][j][e] = v.re;
-          di[i][j][e] = v.im;
+        if constexpr (Sc<T>::cx) {
+          vr[i][j][e] = v.re;
+          vi[i][j][e] = v.im;
         } else {
-          dr[i][j][e] = v;
+          vr[i][j][e] = v;
         }
       }
-  // ---- operands: -C (128 x NB) and P (NB x TC) into shared memory
+}
+
+template <typename T, bool SKEW>
+__global__ void __launch_bounds__(256, 1) lg_dmma_update_kernel(LgArgs<T> A, int r_lo, int c_lo) {
+  constexpr bool CX = Sc<T>::cx;
+  constexpr int NB = LgDm<T>::NB, TC = LgDm<T>::TC, WC = LgDm<T>::WC;
+  constexpr int SA = LgDmSmem<T>::SA, SB = LgDmSmem<T>::SB;
+  constexpr int MT = 4, NT = WC / 8;            // 8 x 8 accumulator tiles of a warp
+  constexpr int PE = NB * TC / 256;             // P entries per thread and tile
+  static_assert(NB * TC % 256 == 0, "P tile shared evenly");
+  extern __shared__ __align__(16) unsigned char lgdm_raw[];
+  LgDmSmem<T>& S = *reinterpret_cast<LgDmSmem<T>*>(lgdm_raw);
+  const int b = blockIdx.z, n = A.n, k0 = A.k0, kw = A.kw;
+  const int r0 = r_lo + blockIdx.y * 128;
+  // this CTA's run of column tiles; the skew update keeps tiles that reach the lower triangle
+  const int c_end = SKEW ? min(n, r0 + 128) : n;
+  int c0 = c_lo + blockIdx.x * (kLgDmTiles * TC);
+  if (c0 >= c_end) return;
+  const int c_stop = min(c_end, c0 + kLgDmTiles * TC);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int wr = r0 + (warp >> 1) * 32;
+  T* Mb = A.M + (size_t)b * n * n;
+  const T* Cb = A.C + (size_t)b * n * NB;
+  const T* Pb = A.P + (size_t)b * NB * n;
+
+  // ---- accumulators = the first M tile (re / im); its P rows and -C into shared memory
+  double dr[MT][NT][2], di[CX ? MT : 1][CX ? NT : 1][2];
+  lg_dm_load_m<T, MT, NT>(Mb, n, wr, c0 + (warp & 1) * WC, g, t, dr, di);
   for (int e = tid; e < 128 * NB; e += 256) {
     const int rr = e / NB, s = e % NB, r = r0 + rr;
     const T v = (r < n && s < kw) ? Cb[(size_t)r * NB + s] : s_zero<T>();
@@ -421,66 +439,101 @@ __global__ void __launch_bounds__(256, 2) lg_dmma_update_kernel(LgArgs<T> A, int
       S.ar[rr * SA + s] = -v;
     }
   }
-  for (int e = tid; e < NB * TC; e += 256) {
-    const int s = e / TC, cc = e % TC, c = c0 + cc;
-    const T v = (c < n && s < kw) ? Pb[(size_t)s * n + c] : s_zero<T>();
-    if constexpr (CX) {
-      S.br[s * SB + cc] = v.re;
-      S.bi[s * SB + cc] = v.im;
-    } else {
-      S.br[s * SB + cc] = v;
-    }
+  T pv[PE];
+#pragma unroll
+  for (int q = 0; q < PE; ++q) {
+    const int e = tid + 256 * q, s = e / TC, c = c0 + e % TC;
+    pv[q] = (c < n && s < kw) ? Pb[(size_t)s * n + c] : s_zero<T>();
   }
-  __syncthreads();
-  // ---- D += (-C) P, K = 4 per step
   const int ar0 = (warp >> 1) * 32, bc0 = (warp & 1) * WC;
 #pragma unroll 1
-  for (int k = 0; k < NB; k += 4) {
-    double a_r[MT], a_i[CX ? MT : 1], b_r[NT], b_i[CX ? NT : 1];
+  for (;;) {
+    // this tile's P rows into shared memory (the previous tile's readers are done)
 #pragma unroll
-    for (int i = 0; i < MT; ++i) {
-      a_r[i] = S.ar[(ar0 + 8 * i + g) * SA + k + t];
-      if constexpr (CX) a_i[i] = S.ai[(ar0 + 8 * i + g) * SA + k + t];
+    for (int q = 0; q < PE; ++q) {
+      const int e = tid + 256 * q, s = e / TC, cc = e % TC;
+      if constexpr (CX) {
+        S.br[s * SB + cc] = pv[q].re;
+        S.bi[s * SB + cc] = pv[q].im;
+      } else {
+        S.br[s * SB + cc] = pv[q];
+      }
     }
+    __syncthreads();
+    // ---- the next tile's M entries and P rows start loading
+    const int cn = c0 + TC;
+    const bool more = cn < c_stop;
+    double nr[MT][NT][2], ni[CX ? MT : 1][CX ? NT : 1][2];
+    if (more) {
+      lg_dm_load_m<T, MT, NT>(Mb, n, wr, cn + (warp & 1) * WC, g, t, nr, ni);
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      b_r[j] = S.br[(k + t) * SB + bc0 + 8 * j + g];
-      if constexpr (CX) b_i[j] = S.bi[(k + t) * SB + bc0 + 8 * j + g];
+      for (int q = 0; q < PE; ++q) {
+        const int e = tid + 256 * q, s = e / TC, c = cn + e % TC;
+        pv[q] = (c < n && s < kw) ? Pb[(size_t)s * n + c] : s_zero<T>();
+      }
     }
+    // ---- D += (-C) P, K = 4 per step
+#pragma unroll 1
+    for (int k = 0; k < NB; k += 4) {
+      double a_r[MT], a_i[CX ? MT : 1], b_r[NT], b_i[CX ? NT : 1];
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        a_r[i] = S.ar[(ar0 + 8 * i + g) * SA + k + t];
+        if constexpr (CX) a_i[i] = S.ai[(ar0 + 8 * i + g) * SA + k + t];
+      }
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        b_r[j] = S.br[(k + t) * SB + bc0 + 8 * j + g];
+        if constexpr (CX) b_i[j] = S.bi[(k + t) * SB + bc0 + 8 * j + g];
+      }
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          dmma(dr[i][j][0], dr[i][j][1], a_r[i], b_r[j]);
+          if constexpr (CX) {
+            // re += (-Cr) Pr - (-Ci) Pi; im += (-Cr) Pi + (-Ci) Pr
+            dmma(dr[i][j][0], dr[i][j][1], -a_i[i], b_i[j]);
+            dmma(di[i][j][0], di[i][j][1], a_r[i], b_i[j]);
+            dmma(di[i][j][0], di[i][j][1], a_i[i], b_r[j]);
+          }
+        }
+    }
+    // ---- store the updated entries
+    const int wc = c0 + bc0;
 #pragma unroll
     for (int i = 0; i < MT; ++i)
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        dmma(dr[i][j][0], dr[i][j][1], a_r[i], b_r[j]);
-        if constexpr (CX) {
-          // re += (-Cr) Pr - (-Ci) Pi; im += (-Cr) Pi + (-Ci) Pr
-          dmma(dr[i][j][0], dr[i][j][1], -a_i[i], b_i[j]);
-          dmma(di[i][j][0], di[i][j][1], a_r[i], b_i[j]);
-          dmma(di[i][j][0], di[i][j][1], a_i[i], b_r[j]);
-        }
-      }
-  }
-  // ---- store the updated entries
+      for (int j = 0; j < NT; ++j)
 #pragma unroll
-  for (int i = 0; i < MT; ++i)
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int rr = wr + 8 * i + g, cc = wc + 8 * j + 2 * t + e;
-        const bool ok = rr < n && cc < n && (cc < k0 || cc >= k0 + kw) && (!SKEW || rr > cc);
-        if (ok) {
-          T v;
-          if constexpr (CX) {
-            v.re = dr[i][j][e];
-            v.im = di[i][j][e];
-          } else {
-            v = dr[i][j][e];
+        for (int e = 0; e < 2; ++e) {
+          const int rr = wr + 8 * i + g, cc = wc + 8 * j + 2 * t + e;
+          const bool ok = rr < n && cc < n && (cc < k0 || cc >= k0 + kw) && (!SKEW || rr > cc);
+          if (ok) {
+            T v;
+            if constexpr (CX) {
+              v.re = dr[i][j][e];
+              v.im = di[i][j][e];
+            } else {
+              v = dr[i][j][e];
+            }
+            Mb[(size_t)rr * n + cc] = v;
+            if (SKEW) Mb[(size_t)cc * n + rr] = neg(v);
           }
-          Mb[(size_t)rr * n + cc] = v;
-          if (SKEW) Mb[(size_t)cc * n + rr] = neg(v);
         }
-      }
+    if (!more) break;
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          dr[i][j][e] = nr[i][j][e];
+          if constexpr (CX) di[i][j][e] = ni[i][j][e];
+        }
+    c0 = cn;
+    __syncthreads();  // every warp is done with this tile's P rows
+  }
 }
 
 }  // namespace fx

@@ -64,7 +64,9 @@ int lg_update(cudaStream_t s, const LgArgs<T>& A, int lo, int cnt, int prec) {
     LgArgs<T> arg = A;
     int r_lo = lo, c_lo = lo;
     void* args[] = {&arg, &r_lo, &c_lo};
-    const dim3 grid((unsigned)((n - lo + TC - 1) / TC), (unsigned)((n - lo + 127) / 128), (unsigned)cnt);
+    // one CTA per run of kLgDmTiles column tiles of a 128-row strip
+    const int tiles = (n - lo + TC - 1) / TC;
+    const dim3 grid((unsigned)((tiles + kLgDmTiles - 1) / kLgDmTiles), (unsigned)((n - lo + 127) / 128), (unsigned)cnt);
     return cudaLaunchKernel(k, grid, dim3(256), args, smem, s) == cudaSuccess ? FX_OK : FX_ERR_CUDA;
   }
   lg_update_kernel<T, SKEW><<<dim3((n - lo + 63) / 64, (n - lo + 63) / 64, cnt), 256, 0, s>>>(A, lo, lo);

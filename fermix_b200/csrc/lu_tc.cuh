@@ -465,6 +465,38 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
       const bool zero = S.nz != 0 || S.bad;
       const float f = J.coef ? J.coef[b] : 1.f;
       float* G = J.g + b * (int64_t)n * n;
+      if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(J.g) & 15) == 0) {
+        // through shared memory (the free operand space): 32 gradient rows at a time are
+        // assembled as gsm[k][pos] (row at[c0 + k]), then written as whole 16-byte pieces of
+        // whole rows, so that the L2 receives whole sectors
+        static_assert(offsetof(LuTcSmemT<NR>, blo) + sizeof(S.blo) == 5 * sizeof(S.chi) &&
+                          sizeof(float) * 32 * (NR + 4) <= 5 * sizeof(S.chi),
+                      "the gradient rows fit the operand space");
+        float(*gsm)[NR + 4] = reinterpret_cast<float(*)[NR + 4]>(S.chi);
+#pragma unroll 1
+        for (int c0 = 0; c0 < n; c0 += 32) {
+          uint32_t w[32];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t t8[8];
+            umma::tmem_ld8(trow + c0 + 8 * q, t8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) w[8 * q + e] = t8[e];
+          }
+          umma::tmem_wait_ld();
+          if (x < n) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) gsm[k][mypos] = zero ? 0.f : f * __uint_as_float(w[k]);
+          }
+          __syncthreads();
+          for (int k = warp; k < 32 && c0 + k < n; k += NW) {
+            float* grow = G + (int64_t)S.at[c0 + k] * n;
+            for (int q = lane; 4 * q < n; q += 32)
+              reinterpret_cast<float4*>(grow)[q] = *reinterpret_cast<const float4*>(&gsm[k][4 * q]);
+          }
+          __syncthreads();
+        }
+      } else {
 #pragma unroll 1
       for (int c0 = 0; c0 < n; c0 += 32) {
         uint32_t w[32];
@@ -481,6 +513,7 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
           for (int k = 0; k < 32; ++k)
             if (c0 + k < n) G[(int64_t)S.at[c0 + k] * n + mypos] = zero ? 0.f : f * __uint_as_float(w[k]);
         }
+      }
       }
     }
     tc_sync();

@@ -141,6 +141,9 @@ static_assert(offsetof(PfTcSmem, whi) == sizeof(PfTcSmem::uv) && offsetof(PfTcSm
                   2 * 32 * kTcStgLd * sizeof(float) <= sizeof(PfTcSmem::uv) + 4 * sizeof(PfTcSmem::whi),
               "the staging buffers fit uv and the operands");
 
+static_assert(4 * 32 * 36 * sizeof(float) <= sizeof(PfTcSmem::uv) + 4 * sizeof(PfTcSmem::whi),
+              "the gradient store's per-warp blocks fit uv and the operands");
+
 // warp 0: rows 32 c .. of the matrix into buffer c & 1 (lane l copies row 32 c + l)
 __device__ __forceinline__ void pf_tc_stage_issue(PfTcSmem& S, const float* src, int n, int c, int lane) {
   const int rows = min(32, n - 32 * c);
@@ -651,7 +654,12 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
       // TMEM = -S^-1: gradient of sum(logabs) = -S^-1 / 2, scaled by coef
       const bool zero = S.cand_f[0] != 0 || S.bad;
       const float f = 0.5f * (J.coef ? J.coef[b] : 1.f);
-      tc_store_rows(J.g + b * (int64_t)n * n, n, f, zero, trow, x);
+      float* G = J.g + b * (int64_t)n * n;
+      if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(J.g) & 15) == 0)
+        // whole-sector stores through a 32 x 36 block per warp in the (now free) uv / operand space
+        tc_store_rows_staged(G, n, f, zero, trow, x, reinterpret_cast<float*>(&S.uv[0][0]) + warp * 32 * 36);
+      else
+        tc_store_rows(G, n, f, zero, trow, x);
     }
     tc_sync();
     FX_TOC(tq, 13);

@@ -174,4 +174,42 @@ __device__ __forceinline__ void tc_store_rows(float* __restrict__ dst, int n, fl
   }
 }
 
+// As tc_store_rows for a 16-byte aligned dst and n % 4 == 0, through this warp's 32 x 36 float
+// block of shared memory (wsm): each lane parks its 32 values of a column chunk as 16-byte
+// stores (conflict-free quarter-warps), then every warp store writes 4 whole 128-byte row
+// pieces, so the L2 receives whole 32-byte sectors instead of halves it might fill from DRAM.
+__device__ __forceinline__ void tc_store_rows_staged(float* __restrict__ dst, int n, float f, bool zero_out,
+                                                     uint32_t trow, int x, float* __restrict__ wsm) {
+  const int lane = x & 31, r0 = x - lane;
+#pragma unroll 1
+  for (int c0 = 0; c0 < n; c0 += 32) {
+    uint32_t w[32];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t t[8];
+      umma::tmem_ld8(trow + c0 + 8 * q, t);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[8 * q + j] = t[j];
+    }
+    umma::tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = zero_out ? 0.f : f * __uint_as_float(w[4 * q + e]);
+      *reinterpret_cast<float4*>(wsm + lane * 36 + 4 * q) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    __syncwarp();
+    const int cq = 4 * (lane & 7);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = 4 * i + (lane >> 3);
+      if (r0 + rr < n && c0 + cq < n)
+        *reinterpret_cast<float4*>(dst + (size_t)(r0 + rr) * n + c0 + cq) =
+            *reinterpret_cast<const float4*>(wsm + rr * 36 + cq);
+    }
+    __syncwarp();
+  }
+}
+
 }  // namespace fx
