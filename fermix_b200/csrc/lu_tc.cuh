@@ -104,7 +104,10 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
       tc_load_gathered<NR>(J.gbase, J.gld, J.grows, J.gidx + b * (int64_t)n, n, trow, x);
     } else {
       const float* src = J.a + b * (int64_t)n * n;
-      if (tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
+      // the forward streams the block's next matrix into L2 meanwhile; the gradient does not
+      // (measured: the gradient writes evicted most prefetched lines before use, reading the
+      // input twice from DRAM)
+      if (!GRAD && tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
       tc_load_matrix<NR>(src, n, false, trow, x);
     }
     int mypos = x < n ? -1 : NR;  // pivot position of this row (-1: not yet pivoted)

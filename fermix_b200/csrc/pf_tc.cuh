@@ -273,10 +273,10 @@ __global__ void __launch_bounds__(128, 4) pf_tc_kernel(Job<float> J) {
 
   for (int64_t b = blockIdx.x; b < J.B; b += gridDim.x) {
     FX_TIC(tq);
-    // ---- the (skew-symmetrised) matrix into TMEM, zero outside n x n; the block's
-    // next matrix starts streaming into L2 meanwhile
+    // ---- the (skew-symmetrised) matrix into TMEM, zero outside n x n. (No L2 prefetch of
+    // the block's next matrix: measured, its lines were mostly evicted by the gradient
+    // writes before use, reading the input twice from DRAM.)
     const float* src = J.a + b * (int64_t)n * n;
-    if (tid == 0 && b + gridDim.x < J.B) tc_prefetch_l2(src + (int64_t)gridDim.x * n * n, n);
     if (tid == 0) S.bad = 0;
     if (staged) {
       __syncthreads();  // S.bad cleared before a chunk wait can set it
