@@ -243,14 +243,59 @@ struct PflClSlot {
   T val[2], fval[2];
 };
 
-template <typename T, int CL>
-__global__ void __launch_bounds__(kPflRows) pfl_panel_cl_kernel(PflArgs<T> A) {
+// Column x of the pivot row's pair corrections: col += tau_x w_r - w_x tau_r over this panel's
+// earlier pairs t < s, the pivot row's factors (w_r, tau_r) read from block `rank`. BATCH (the
+// 512-row blocks, 128 registers a thread): four pairs' remote reads are issued before the
+// first is used; otherwise one pair's two reads at a time (the 1024-row blocks' 64 registers).
+template <typename T, int NP, bool BATCH>
+__device__ __forceinline__ T pfl_cl_correct(T col, const T* Wr, uint32_t rank, int s, const T* Wme, bool have) {
+  if constexpr (BATCH) {
+    // groups of four pairs: eight remote reads in flight, then their FMAs
+    const uint32_t base = cl_map(Wr, rank);
+#pragma unroll
+    for (int t0 = 0; t0 < NP; t0 += 4) {
+      if (t0 < s) {
+        T w[4], tau[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (t0 + j < s) {
+            w[j] = cl_ld(base + (uint32_t)(2 * (t0 + j) * sizeof(T)), (T*)nullptr);
+            tau[j] = cl_ld(base + (uint32_t)((2 * (t0 + j) + 1) * sizeof(T)), (T*)nullptr);
+          }
+        }
+        if (have) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (t0 + j < s) {
+              col = fma_(Wme[2 * (t0 + j) + 1], w[j], col);
+              col = fms(col, Wme[2 * (t0 + j)], tau[j]);
+            }
+          }
+        }
+      }
+    }
+  } else {
+    for (int t = 0; t < s; ++t) {
+      const T w = cl_get(Wr + 2 * t, rank), tau = cl_get(Wr + 2 * t + 1, rank);
+      if (have) {
+        col = fma_(Wme[2 * t + 1], w, col);
+        col = fms(col, Wme[2 * t], tau);
+      }
+    }
+  }
+  return col;
+}
+
+// ROWS rows per block (512 or 1024), NP pairs per panel, CL * ROWS >= n - k0.
+template <typename T, int CL, int ROWS, int NP>
+__global__ void __launch_bounds__(ROWS) pfl_panel_cl_kernel(PflArgs<T> A) {
   typedef typename Sc<T>::R R;
-  constexpr int NP = PflCfg<T>::NP, WL = 2 * NP + 1;
-  constexpr int NW = kPflRows / 32;
+  constexpr int WL = 2 * NP + 1;
+  constexpr int NW = ROWS / 32;
+  static_assert(NW <= 32, "one warp merges the block's warp candidates");
   extern __shared__ __align__(16) unsigned char smem[];
-  T* W = reinterpret_cast<T*>(smem);                               // [1024][WL] this block's rows
-  PflClSlot<T>* cs = reinterpret_cast<PflClSlot<T>*>(W + (size_t)kPflRows * WL);  // block candidate
+  T* W = reinterpret_cast<T*>(smem);                               // [ROWS][WL] this block's rows
+  PflClSlot<T>* cs = reinterpret_cast<PflClSlot<T>*>(W + (size_t)ROWS * WL);  // block candidate
   T* wval = reinterpret_cast<T*>(cs + 1);                          // [2][NW] warp candidates' values
   R* wkey = reinterpret_cast<R*>(wval + 2 * NW);                   // [NW]
   int* wrow = reinterpret_cast<int*>(wkey + NW);                   // [NW]
@@ -261,10 +306,10 @@ __global__ void __launch_bounds__(kPflRows) pfl_panel_cl_kernel(PflArgs<T> A) {
   const int b = blockIdx.x / CL, n = A.n, k0 = A.k0, np = A.np;
   const int m = n - k0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int xr = (int)rank * kPflRows + tid;  // this thread's row offset
+  const int xr = (int)rank * ROWS + tid;  // this thread's row offset
   const bool have = xr < m;
   T* Mb = A.M + (size_t)b * n * n;
-  for (int i = tid; i < m; i += kPflRows) {
+  for (int i = tid; i < m; i += ROWS) {
     at[i] = i;
     pof[i] = i;
   }
@@ -274,18 +319,10 @@ __global__ void __launch_bounds__(kPflRows) pfl_panel_cl_kernel(PflArgs<T> A) {
     const int par = s & 1;
     const int c = 2 * s;
     const int a = at[c];
-    const uint32_t ao = (uint32_t)(a / kPflRows);
-    const T* Wa = W + (a % kPflRows) * WL;
     if (xr == a) unas = false;
     T colA = s_zero<T>();
     if (have) colA = Mb[(size_t)(k0 + xr) * n + k0 + a];
-    for (int t = 0; t < s; ++t) {
-      const T wa = cl_get(Wa + 2 * t, ao), ta = cl_get(Wa + 2 * t + 1, ao);
-      if (have) {
-        colA = fma_(W[tid * WL + 2 * t + 1], wa, colA);
-        colA = fms(colA, W[tid * WL + 2 * t], ta);
-      }
-    }
+    colA = pfl_cl_correct<T, NP, (ROWS <= 512)>(colA, W + (a % ROWS) * WL, (uint32_t)(a / ROWS), s, W + tid * WL, have);
     R best = unas ? abs1(colA) : R(-1);
     if (!(best >= R(0))) best = R(-1);
     int bi = (unas && best >= R(0)) ? xr : 0x7fffffff;
@@ -318,12 +355,13 @@ __global__ void __launch_bounds__(kPflRows) pfl_panel_cl_kernel(PflArgs<T> A) {
     }
     __syncthreads();
     if (warp == 0) {
-      // this block's candidate: lane w takes warp w's (NW == 32)
-      best = wkey[lane];
-      bi = wrow[lane];
-      bv = wval[lane];
-      fi = wfi[lane];
-      fv = wval[NW + lane];
+      // this block's candidate: lane w takes warp w's (lanes past the block's warps hold none)
+      const bool in = lane < NW;
+      best = in ? wkey[lane] : R(-1);
+      bi = in ? wrow[lane] : 0x7fffffff;
+      bv = in ? wval[lane] : s_zero<T>();
+      fi = in ? wfi[lane] : 0x7fffffff;
+      fv = in ? wval[NW + lane] : s_zero<T>();
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
         const R ob = __shfl_xor_sync(0xffffffffu, best, off);
@@ -376,17 +414,9 @@ __global__ void __launch_bounds__(kPflRows) pfl_panel_cl_kernel(PflArgs<T> A) {
     const T d = neg(pv);
     const T inv = recip(d);
     if (xr == p) unas = false;
-    const uint32_t po = (uint32_t)(p / kPflRows);
-    const T* Wp = W + (p % kPflRows) * WL;
     T colP = s_zero<T>();
     if (have) colP = Mb[(size_t)(k0 + xr) * n + k0 + p];
-    for (int t = 0; t < s; ++t) {
-      const T wp = cl_get(Wp + 2 * t, po), tp = cl_get(Wp + 2 * t + 1, po);
-      if (have) {
-        colP = fma_(W[tid * WL + 2 * t + 1], wp, colP);
-        colP = fms(colP, W[tid * WL + 2 * t], tp);
-      }
-    }
+    colP = pfl_cl_correct<T, NP, (ROWS <= 512)>(colP, W + (p % ROWS) * WL, (uint32_t)(p / ROWS), s, W + tid * WL, have);
     if (have) {
       W[tid * WL + 2 * s] = unas ? colP : s_zero<T>();
       W[tid * WL + 2 * s + 1] = unas ? neg(mul(colA, inv)) : s_zero<T>();
@@ -409,6 +439,7 @@ __global__ void __launch_bounds__(kPflRows) pfl_panel_cl_kernel(PflArgs<T> A) {
   }
   if (have) {
     constexpr int LD = LgCfg<T>::NB;
+    static_assert(2 * NP <= LD, "the update operands hold 2 NP columns");
     const int pos = k0 + pof[xr];
     T* cr = A.C + ((size_t)b * n + pos) * LD;
     T* pb = A.P + (size_t)b * LD * n;
@@ -424,13 +455,21 @@ __global__ void __launch_bounds__(kPflRows) pfl_panel_cl_kernel(PflArgs<T> A) {
   }
 }
 
-template <typename T>
+template <typename T, int ROWS, int NP>
 inline size_t pfl_panel_cl_smem() {
   typedef typename Sc<T>::R R;
-  constexpr int NW = kPflRows / 32;
-  return (size_t)kPflRows * (2 * PflCfg<T>::NP + 1) * sizeof(T) + sizeof(PflClSlot<T>) + 2 * NW * sizeof(T) +
-         NW * sizeof(R) + 2 * NW * sizeof(int) + 2 * kPflMaxN * sizeof(int) + 64;
+  constexpr int NW = ROWS / 32;
+  return (size_t)ROWS * (2 * NP + 1) * sizeof(T) + sizeof(PflClSlot<T>) + 2 * NW * sizeof(T) + NW * sizeof(R) +
+         2 * NW * sizeof(int) + 2 * kPflMaxN * sizeof(int) + 64;
 }
+
+// complex128 panels of 8 pairs (the update kernel's full K = 16) on 512-row cluster blocks,
+// for n - k0 <= 8 * 512; wider trailing blocks keep 4 pairs on 1024-row blocks
+template <typename T>
+struct PflWide {
+  static constexpr bool on = std::is_same<T, c128_t>::value;
+  static constexpr int ROWS = 512, NP = LgCfg<T>::NB / 2, MAXM = 8 * ROWS;
+};
 
 // 2a. the panel's row interchanges on columns [k0, n)
 template <typename T>

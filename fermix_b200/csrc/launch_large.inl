@@ -175,16 +175,16 @@ int run_large_lu(cudaStream_t s, Job<T> J, void* ws, size_t wsb, bool grad, bool
   return FX_OK;
 }
 
-// Cluster launch of the split panel: CL blocks of 1024 threads per matrix.
-template <typename T, int CL>
+// Cluster launch of the split panel: CL blocks of ROWS threads per matrix, NP pairs.
+template <typename T, int CL, int ROWS, int NP>
 int launch_pfl_cl(cudaStream_t s, const PflArgs<T>& A, int cnt) {
-  const size_t smem = pfl_panel_cl_smem<T>();
-  void* k = (void*)&pfl_panel_cl_kernel<T, CL>;
+  const size_t smem = pfl_panel_cl_smem<T, ROWS, NP>();
+  void* k = (void*)&pfl_panel_cl_kernel<T, CL, ROWS, NP>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return FX_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(CL * cnt));
-  cfg.blockDim = dim3(kPflRows);
+  cfg.blockDim = dim3(ROWS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
@@ -224,35 +224,58 @@ int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
   U.P = A.P;
   U.n = n;
   U.wait_polls = J.wait_polls;
-  // n <= 512: 512-row panel blocks with twice the pairs (a wider, less memory-bound update)
+  // n <= 512: 512-row panel blocks with twice the pairs (a wider, less memory-bound update);
+  // complex128 also takes 8-pair panels on 512-row cluster blocks while n - k0 <= 4096
   const bool small = n <= 512;
   constexpr int NPS = PflCfg<T>::NP_SMALL;
-  const int np_max = small ? NPS : NP;
+  using Wd = PflWide<T>;
   const size_t psmem = small ? pfl_panel_smem<T, NPS, 512>() : pfl_panel_smem<T, NP, kPflRows>();
   void* pk = small ? (void*)&pfl_panel_kernel<T, NPS, 512> : (void*)&pfl_panel_kernel<T, NP, kPflRows>;
   if (cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) != cudaSuccess)
     return FX_ERR_CUDA;
+  if (Wd::on) {
+    void* wk = (void*)&pfl_panel_kernel<T, NPS, 512>;
+    if (cudaFuncSetAttribute(wk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pfl_panel_smem<T, NPS, 512>()) !=
+        cudaSuccess)
+      return FX_ERR_CUDA;
+  }
   for (int64_t b0 = 0; b0 < J.B; b0 += bs) {
     const int cnt = (int)(J.B - b0 < bs ? J.B - b0 : bs);
     if (lg_copy_in<T>(s, A.M, J, b0, cnt, n, J.skew)) return FX_ERR_CUDA;
-    for (int k0 = 0; k0 < n; k0 += 2 * np_max) {
-      A.k0 = k0;
-      A.np = (n - k0) / 2 < np_max ? (n - k0) / 2 : np_max;
+    for (int k0 = 0; k0 < n;) {
       const int m = n - k0;
-      if (small) {
-        pfl_panel_kernel<T, NPS, 512><<<cnt, 512, psmem, s>>>(A);
+      const bool wide = Wd::on && !small && m <= Wd::MAXM;
+      const int np_max = small ? NPS : (wide ? Wd::NP : NP);
+      A.k0 = k0;
+      A.np = m / 2 < np_max ? m / 2 : np_max;
+      if (small || (wide && m <= 512)) {
+        pfl_panel_kernel<T, NPS, 512><<<cnt, 512, pfl_panel_smem<T, NPS, 512>(), s>>>(A);
+      } else if (wide) {
+        int e = FX_ERR_SHAPE;
+        if constexpr (PflWide<T>::on) {
+          switch ((m + Wd::ROWS - 1) / Wd::ROWS) {
+            case 2: e = launch_pfl_cl<T, 2, Wd::ROWS, Wd::NP>(s, A, cnt); break;
+            case 3: e = launch_pfl_cl<T, 3, Wd::ROWS, Wd::NP>(s, A, cnt); break;
+            case 4: e = launch_pfl_cl<T, 4, Wd::ROWS, Wd::NP>(s, A, cnt); break;
+            case 5: e = launch_pfl_cl<T, 5, Wd::ROWS, Wd::NP>(s, A, cnt); break;
+            case 6: e = launch_pfl_cl<T, 6, Wd::ROWS, Wd::NP>(s, A, cnt); break;
+            case 7: e = launch_pfl_cl<T, 7, Wd::ROWS, Wd::NP>(s, A, cnt); break;
+            case 8: e = launch_pfl_cl<T, 8, Wd::ROWS, Wd::NP>(s, A, cnt); break;
+          }
+        }
+        if (e) return e;
       } else if (m <= kPflRows) {
         pfl_panel_kernel<T, NP, kPflRows><<<cnt, kPflRows, psmem, s>>>(A);
       } else {
         int e = FX_ERR_SHAPE;
         switch ((m + kPflRows - 1) / kPflRows) {
-          case 2: e = launch_pfl_cl<T, 2>(s, A, cnt); break;
-          case 3: e = launch_pfl_cl<T, 3>(s, A, cnt); break;
-          case 4: e = launch_pfl_cl<T, 4>(s, A, cnt); break;
-          case 5: e = launch_pfl_cl<T, 5>(s, A, cnt); break;
-          case 6: e = launch_pfl_cl<T, 6>(s, A, cnt); break;
-          case 7: e = launch_pfl_cl<T, 7>(s, A, cnt); break;
-          case 8: e = launch_pfl_cl<T, 8>(s, A, cnt); break;
+          case 2: e = launch_pfl_cl<T, 2, kPflRows, NP>(s, A, cnt); break;
+          case 3: e = launch_pfl_cl<T, 3, kPflRows, NP>(s, A, cnt); break;
+          case 4: e = launch_pfl_cl<T, 4, kPflRows, NP>(s, A, cnt); break;
+          case 5: e = launch_pfl_cl<T, 5, kPflRows, NP>(s, A, cnt); break;
+          case 6: e = launch_pfl_cl<T, 6, kPflRows, NP>(s, A, cnt); break;
+          case 7: e = launch_pfl_cl<T, 7, kPflRows, NP>(s, A, cnt); break;
+          case 8: e = launch_pfl_cl<T, 8, kPflRows, NP>(s, A, cnt); break;
         }
         if (e) return e;
       }
@@ -264,6 +287,7 @@ int run_large_pf(cudaStream_t s, Job<T> J, void* ws, size_t wsb) {
         U.kw = 2 * A.np;
         if (int e = lg_update<T, true>(s, U, lo, cnt, J.prec)) return e;
       }
+      k0 = lo;
     }
     pfl_finish_kernel<T><<<cnt, 32, 0, s>>>(A, J, b0);
     if (cudaGetLastError() != cudaSuccess) return FX_ERR_CUDA;
