@@ -11,7 +11,9 @@
 //   1. pfl_panel_kernel: one block per matrix, thread x owns the row at position k0 + x.
 //      Pair step s reads the corrected columns a and p of the current matrix (the stored
 //      column plus this panel's earlier pair corrections, the same FMA chains as the
-//      register-panel kernel) with virtual pivoting, and keeps each row's pair factors
+//      register-panel kernel) with virtual pivoting; the trailing block is kept exactly skew
+//      (mirrored updates, symmetric interchanges), so column a is read as minus row a, one
+//      coalesced row instead of a strided column, and keeps each row's pair factors
 //      (w_t, tau_t) in shared memory; at the end the factors go out by final position as
 //      the update operands C = (-tau_t, w_t) and P = (w_t; tau_t);
 //   2. pfl_swap_rows_kernel / pfl_swap_cols_kernel: the panel's symmetric interchanges
@@ -76,7 +78,7 @@ __global__ void __launch_bounds__(ROWS) pfl_panel_kernel(PflArgs<T> A) {
     // column a of the current matrix at this row, with the panel's earlier corrections
     T colA = s_zero<T>();
     if (have) {
-      colA = Mb[(size_t)(k0 + x) * n + k0 + a];
+      colA = neg(Mb[(size_t)(k0 + a) * n + k0 + x]);  // S[x][a] = -S[a][x]: row a, coalesced
       for (int t = 0; t < s; ++t) {
         colA = fma_(W[x * WL + 2 * t + 1], W[a * WL + 2 * t], colA);
         colA = fms(colA, W[x * WL + 2 * t], W[a * WL + 2 * t + 1]);
@@ -141,7 +143,7 @@ __global__ void __launch_bounds__(ROWS) pfl_panel_kernel(PflArgs<T> A) {
     const T inv = recip(d);
     if (x == p) unas = false;
     if (have) {
-      T colP = Mb[(size_t)(k0 + x) * n + k0 + p];
+      T colP = neg(Mb[(size_t)(k0 + p) * n + k0 + x]);
       for (int t = 0; t < s; ++t) {
         colP = fma_(W[x * WL + 2 * t + 1], W[p * WL + 2 * t], colP);
         colP = fms(colP, W[x * WL + 2 * t], W[p * WL + 2 * t + 1]);
@@ -321,7 +323,7 @@ __global__ void __launch_bounds__(ROWS) pfl_panel_cl_kernel(PflArgs<T> A) {
     const int a = at[c];
     if (xr == a) unas = false;
     T colA = s_zero<T>();
-    if (have) colA = Mb[(size_t)(k0 + xr) * n + k0 + a];
+    if (have) colA = neg(Mb[(size_t)(k0 + a) * n + k0 + xr]);  // S[x][a] = -S[a][x]: row a, coalesced
     colA = pfl_cl_correct<T, NP, (ROWS <= 512)>(colA, W + (a % ROWS) * WL, (uint32_t)(a / ROWS), s, W + tid * WL, have);
     R best = unas ? abs1(colA) : R(-1);
     if (!(best >= R(0))) best = R(-1);
@@ -415,7 +417,7 @@ __global__ void __launch_bounds__(ROWS) pfl_panel_cl_kernel(PflArgs<T> A) {
     const T inv = recip(d);
     if (xr == p) unas = false;
     T colP = s_zero<T>();
-    if (have) colP = Mb[(size_t)(k0 + xr) * n + k0 + p];
+    if (have) colP = neg(Mb[(size_t)(k0 + p) * n + k0 + xr]);
     colP = pfl_cl_correct<T, NP, (ROWS <= 512)>(colP, W + (p % ROWS) * WL, (uint32_t)(p / ROWS), s, W + tid * WL, have);
     if (have) {
       W[tid * WL + 2 * s] = unas ? colP : s_zero<T>();
