@@ -471,8 +471,10 @@ __global__ void __launch_bounds__(256) lg_coef_kernel(LgArgs<T> A, int r_lo) {
 // minus the panel columns [k0, k0 + kw); 64 x 64 tiles, 256 threads, 4 x 4 entries per
 // thread, one FMA chain per entry in panel-column order. SKEW: only entries below the
 // diagonal are computed, and M[y][x] = -M[x][y] is written beside them.
+// Four 256-thread blocks per SM for the 4- and 8-byte types: more loads of M in flight (the
+// kernel is bound by their latency).
 template <typename T, bool SKEW = false>
-__global__ void __launch_bounds__(256) lg_update_kernel(LgArgs<T> A, int r_lo, int c_lo) {
+__global__ void __launch_bounds__(256, sizeof(T) <= 8 ? 4 : 2) lg_update_kernel(LgArgs<T> A, int r_lo, int c_lo) {
   constexpr int NB = LgCfg<T>::NB;
   constexpr int TM = 64, TN = 64;
   __shared__ T sC[TM][NB + 1];

@@ -69,6 +69,10 @@ int lg_update(cudaStream_t s, const LgArgs<T>& A, int lo, int cnt, int prec) {
     const dim3 grid((unsigned)((tiles + kLgDmTiles - 1) / kLgDmTiles), (unsigned)((n - lo + 127) / 128), (unsigned)cnt);
     return cudaLaunchKernel(k, grid, dim3(256), args, smem, s) == cudaSuccess ? FX_OK : FX_ERR_CUDA;
   }
+  // the largest shared-memory carveout, so that four blocks' tiles fit beside each other
+  if (cudaFuncSetAttribute(lg_update_kernel<T, SKEW>, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
+      cudaSuccess)
+    return FX_ERR_CUDA;
   lg_update_kernel<T, SKEW><<<dim3((n - lo + 63) / 64, (n - lo + 63) / 64, cnt), 256, 0, s>>>(A, lo, lo);
   return cudaGetLastError() == cudaSuccess ? FX_OK : FX_ERR_CUDA;
 }
