@@ -59,8 +59,9 @@ def _as_real(t):
 def all_gather_slog(sign, logabs, batch, group=None):
     """Concatenate every rank's (sign, logabs) slices, in rank order, into the global
     (batch,) arrays on every rank. The slices must follow shard_bounds(batch, world, .);
-    each rank may hold a different number (zero included). One all-gather per array, of
-    the largest slice, zero-padded."""
+    each rank may hold a different number (zero included). One all-gather of the largest
+    slice, zero-padded, with sign (as real parts) and logabs packed side by side in one
+    buffer of logabs' real dtype."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
@@ -69,16 +70,18 @@ def all_gather_slog(sign, logabs, batch, group=None):
     if sign.shape[0] != counts[rank] or logabs.shape[0] != counts[rank]:
         raise ValueError(f"rank {rank} holds {sign.shape[0]} results, its slice has {counts[rank]}")
     m = max(counts) if counts else 0
-    out = []
-    for t in (sign, logabs):
-        pad = torch.zeros((m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
-        pad[: t.shape[0]] = t
-        parts = [torch.empty_like(_as_real(pad)) for _ in range(world)]
-        dist.all_gather(parts, _as_real(pad).contiguous(), group=group)
-        if t.is_complex():
-            parts = [torch.view_as_complex(p) for p in parts]
-        out.append(torch.cat([p[:c] for p, c in zip(parts, counts)]))
-    return out[0], out[1]
+    ws = 2 if sign.is_complex() else 1
+    sr = _as_real(sign).reshape(sign.shape[0], ws)
+    pack = torch.zeros((m, ws + 1), dtype=logabs.dtype, device=logabs.device)
+    pack[: sign.shape[0], :ws] = sr.to(logabs.dtype)
+    pack[: sign.shape[0], ws] = logabs
+    full = torch.empty((world * m, ws + 1), dtype=pack.dtype, device=pack.device)
+    dist.all_gather_into_tensor(full, pack, group=group)
+    if any(c != m for c in counts):
+        full = torch.cat([full[r * m: r * m + c] for r, c in enumerate(counts)])
+    S = full[:, :ws].contiguous()
+    S = torch.view_as_complex(S) if sign.is_complex() else S.reshape(-1).to(sign.dtype)
+    return S, full[:, ws].contiguous()
 
 
 def dist_slog(op, a_local, batch, *, group=None, **kw):
