@@ -33,14 +33,15 @@ TC_KERNEL = {"slogpf": "pf_tc_kernel", "slogdet": "lu_tc_kernel"}
 
 
 def kernel_name(a):
-    """The dominant kernel of this workload: the tensor-memory kernels for float32 /
-    tf32x3 (slogpf 8 <= n <= 128, even n; slogdet 8 <= n <= 256), the register-panel
-    kernels otherwise up to n = 256, and above that the blocked engines' trailing update
-    (tcgen05 for float32 / complex64 under tf32x3, DMMA for complex128, FMA tiles otherwise)."""
-    if a.dtype == "f32" and a.prec == "tf32x3" and a.n >= 8:
+    """The dominant kernel of this workload: the tensor-memory kernels for float32 (slogpf
+    8 <= n <= 128, even n, both precisions: tcgen05 block updates under tf32x3, FMA ones
+    under ieee; slogdet 8 <= n <= 256 under tf32x3), the register-panel kernels otherwise up
+    to n = 256, and above that the blocked engines' trailing update (tcgen05 for float32 /
+    complex64 under tf32x3, DMMA for complex128, FMA tiles otherwise)."""
+    if a.dtype == "f32" and a.n >= 8:
         if a.op == "slogpf" and a.n <= 128 and a.n % 2 == 0:
             return TC_KERNEL[a.op]
-        if a.op == "slogdet" and a.n <= 256:
+        if a.op == "slogdet" and a.n <= 256 and a.prec == "tf32x3":
             return TC_KERNEL[a.op]
     if a.n <= 256:
         return SMALL_KERNEL[a.op]
@@ -124,7 +125,8 @@ def peaks():
 def traffic_from_profiles(a):
     """DRAM bytes per launch of the dominant kernel: the committed ncu summary's line
     'traffic_bytes_per_matrix: X' for this workload, times the batch; else None."""
-    name = f"{kernel_name(a)}_{a.dtype}_n{a.n}_{'fwd' if a.fwd_only else 'fwdbwd'}.md"
+    ieee = "_ieee" if a.prec == "ieee" and a.dtype in ("f32", "c64") else ""
+    name = f"{kernel_name(a)}_{a.dtype}_n{a.n}{ieee}_{'fwd' if a.fwd_only else 'fwdbwd'}.md"
     p = os.path.join(ROOT, "profiles", name)
     if a.gather or not os.path.exists(p):
         return None
@@ -517,8 +519,9 @@ def compute_roofline(a, flops_per_launch, launch_s, dev):
     kern = kernel_name(a)
     pk = pipe_peaks(dev)
     achieved = flops_per_launch / launch_s / 1e12
-    if kern in TC_KERNEL.values():
-        products = 4 if a.op == "slogdet" else 3
+    if (kern in TC_KERNEL.values() and a.prec == "tf32x3") or kern == "lg_tc_update_kernel":
+        # the LU kernels and the blocked engines' update take 4 TF32 products, pf_tc 3
+        products = 3 if kern == TC_KERNEL["slogpf"] else 4
         pipe, peak = f"tcgen05 kind::tf32, {products} products per update (measured TF32 / {products})", \
             pk["tf32"] / products
     elif a.dtype in ("f32", "c64"):
