@@ -381,6 +381,7 @@ int run_gather(cudaStream_t s, int prec, int64_t batch, int64_t n, const void* p
   const int mode = grad ? MODE_SLOG_GRAD : MODE_FWD;
   if (gather_direct<T>(prec, n, mode)) {
     Job<T> J = make_job<T>(batch, n, nullptr, coef, conj_out, 0, mode, sign, logabs, value, grad);
+    J.prec = prec;  // the tensor-memory LU's update kind (tensor cores or IEEE FMAs)
     J.gidx = occ;
     J.gbase = static_cast<const T*>(phi);
     J.gld = ld;

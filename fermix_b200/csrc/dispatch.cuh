@@ -91,7 +91,8 @@ inline bool use_pf_tc(int dtype_is_f32, int prec, int n, int mode) {
   return dtype_is_f32 && n >= 8 && n <= kTcN && (mode == MODE_FWD || mode == MODE_SLOG_GRAD);
 }
 inline bool use_lu_tc(int dtype_is_f32, int prec, int n, int mode) {
-  return dtype_is_f32 && prec != FX_PREC_IEEE && n >= 8 && n <= 2 * kTcN &&
+  (void)prec;  // tf32x3 and ieee both (tensor-core or FMA block updates)
+  return dtype_is_f32 && n >= 8 && n <= 2 * kTcN &&
          (mode == MODE_FWD || mode == MODE_SLOG_GRAD);
 }
 int launch_pf_tc(cudaStream_t s, Job<float> J);

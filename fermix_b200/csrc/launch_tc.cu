@@ -1,5 +1,6 @@
-// Tensor-memory (tcgen05) kernels: float32, slogpf n <= 128 (prec tf32x3 and ieee) and
-// slogdet n <= 256 (prec tf32x3), forward and slogdet / slogpf gradient.
+// Tensor-memory (tcgen05) kernels: float32, slogpf n <= 128 and slogdet n <= 256 (prec tf32x3:
+// tensor-core block updates; prec ieee: FMA block updates), forward and slogdet / slogpf
+// gradient.
 #include "dispatch.cuh"
 #include "lu_tc.cuh"
 #include "pf_tc.cuh"
@@ -46,9 +47,14 @@ static_assert(sizeof(LuTcSmemT<256>) <= kLuTc256Smem, "LuTcSmemT<256> too large"
 int launch_lu_tc(cudaStream_t s, Job<float> J) {
   const DevInfo* D = dev_info();
   if (!D) return FX_ERR_DEVICE;
-  const bool big = J.n > kTcN;
-  void* k = big ? (J.mode == MODE_FWD ? (void*)&lu_tc_kernel<256, false> : (void*)&lu_tc_kernel<256, true>)
-                : (J.mode == MODE_FWD ? (void*)&lu_tc_kernel<128, false> : (void*)&lu_tc_kernel<128, true>);
+  const bool big = J.n > kTcN, fwd = J.mode == MODE_FWD;
+  void* k;
+  if (J.prec == FX_PREC_IEEE)
+    k = big ? (fwd ? (void*)&lu_tc_kernel<256, false, true> : (void*)&lu_tc_kernel<256, true, true>)
+            : (fwd ? (void*)&lu_tc_kernel<128, false, true> : (void*)&lu_tc_kernel<128, true, true>);
+  else
+    k = big ? (fwd ? (void*)&lu_tc_kernel<256, false> : (void*)&lu_tc_kernel<256, true>)
+            : (fwd ? (void*)&lu_tc_kernel<128, false> : (void*)&lu_tc_kernel<128, true>);
   const size_t smem = big ? kLuTc256Smem : kLuTcSmem;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return FX_ERR_CUDA;

@@ -65,6 +65,14 @@ struct LuTcSmemT {
 };
 using LuTcSmem = LuTcSmemT<128>;
 
+// prec ieee: B's rows (16 values, 80-byte rows: conflict-free 16-byte stores) in the space of
+// the tensor-core operands chi / clo, which that mode does not use
+template <int NR>
+__device__ __forceinline__ float (*lu_tc_brow(LuTcSmemT<NR>& S))[20] {
+  static_assert(sizeof(float) * NR * 20 <= 2 * sizeof(S.chi), "brow fits chi + clo");
+  return reinterpret_cast<float (*)[20]>(S.chi);
+}
+
 // value == hi + mid + lo exactly, each part a TF32 number (hi, mid round to nearest)
 __device__ __forceinline__ void split3(float v, float& hi, float& mid, float& lo) {
   hi = umma::tf32_round(v);
@@ -74,7 +82,53 @@ __device__ __forceinline__ void split3(float v, float& hi, float& mid, float& lo
 }
 
 
-template <int NR, bool GRAD>
+// prec ieee: D -= C B^T on this thread's TMEM row with IEEE float32 FMAs (one sequential chain
+// per entry over the panel's 16 columns), C = this row's coefficients, B's rows (brow, 80-byte
+// rows in the space of the tensor-core operands) broadcast from shared memory; 16 columns per
+// TMEM round trip, from column c_lo on.
+template <int NR>
+__device__ __forceinline__ void lu_tc_fma_update(const float (*brow)[20], uint32_t trow, int n, int c_lo,
+                                                 const float (&c)[16]) {
+#pragma unroll 1
+  for (int c0 = c_lo & ~15; c0 < n; c0 += 16) {
+    uint32_t w0[8], w1[8];
+    umma::tmem_ld8(trow + c0, w0);
+    umma::tmem_ld8(trow + c0 + 8, w1);
+    umma::tmem_wait_ld();
+    float v[16];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      v[e] = __uint_as_float(w0[e]);
+      v[e + 8] = __uint_as_float(w1[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      if (c0 + e < n) {
+        const float4* b4 = reinterpret_cast<const float4*>(brow[c0 + e]);
+        float acc = v[e];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 b = b4[q];
+          acc = fmaf(-c[4 * q], b.x, acc);
+          acc = fmaf(-c[4 * q + 1], b.y, acc);
+          acc = fmaf(-c[4 * q + 2], b.z, acc);
+          acc = fmaf(-c[4 * q + 3], b.w, acc);
+        }
+        v[e] = acc;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      w0[e] = __float_as_uint(v[e]);
+      w1[e] = __float_as_uint(v[e + 8]);
+    }
+    umma::tmem_st8(trow + c0, w0);
+    umma::tmem_st8(trow + c0 + 8, w1);
+  }
+  umma::tmem_wait_st();
+}
+
+template <int NR, bool GRAD, bool IEEE = false>
 __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float> J) {
   constexpr int NW = NR / 32;
   constexpr uint32_t kCols = NR == 128 ? 128u : 512u;  // TMEM columns allocated
@@ -336,17 +390,19 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
             if (t == j) c[t] += 1.f;
         }
       }
+      if (!IEEE) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t off = umma::kmajor_offset(x, 4 * q, kSlab) / 4;
-        float h[4], l[4];
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t off = umma::kmajor_offset(x, 4 * q, kSlab) / 4;
+          float h[4], l[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          h[e] = umma::tf32_round(c[4 * q + e]);
-          l[e] = umma::tf32_round(c[4 * q + e] - h[e]);
+          for (int e = 0; e < 4; ++e) {
+            h[e] = umma::tf32_round(c[4 * q + e]);
+            l[e] = umma::tf32_round(c[4 * q + e] - h[e]);
+          }
+          *reinterpret_cast<float4*>(&S.chi[off]) = make_float4(h[0], h[1], h[2], h[3]);
+          *reinterpret_cast<float4*>(&S.clo[off]) = make_float4(l[0], l[1], l[2], l[3]);
         }
-        *reinterpret_cast<float4*>(&S.chi[off]) = make_float4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<float4*>(&S.clo[off]) = make_float4(l[0], l[1], l[2], l[3]);
       }
       // ---- B operand (K-major): column y = x of the pivot rows, -e_t on the panel
       // columns (forward mode: the columns up to the panel's end stay zero)
@@ -360,15 +416,22 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
           if (y >= k0 && y < k0 + kw) v[t] = (t < kw && y - k0 == t) ? -1.f : 0.f;
           if (zero_col) v[t] = 0.f;
         }
+        if (IEEE) {
+          // row y of B for the FMA update, unsplit
+          float4* b4 = reinterpret_cast<float4*>(lu_tc_brow<NR>(S)[y]);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t off = umma::kmajor_offset(y, 4 * q, kSlab) / 4;
-          float h[4], m[4], l[4];
+          for (int q = 0; q < 4; ++q) b4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        } else {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) split3(v[4 * q + e], h[e], m[e], l[e]);
-          *reinterpret_cast<float4*>(&S.bhi[off]) = make_float4(h[0], h[1], h[2], h[3]);
-          *reinterpret_cast<float4*>(&S.bmid[off]) = make_float4(m[0], m[1], m[2], m[3]);
-          *reinterpret_cast<float4*>(&S.blo[off]) = make_float4(l[0], l[1], l[2], l[3]);
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t off = umma::kmajor_offset(y, 4 * q, kSlab) / 4;
+            float h[4], m[4], l[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) split3(v[4 * q + e], h[e], m[e], l[e]);
+            *reinterpret_cast<float4*>(&S.bhi[off]) = make_float4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<float4*>(&S.bmid[off]) = make_float4(m[0], m[1], m[2], m[3]);
+            *reinterpret_cast<float4*>(&S.blo[off]) = make_float4(l[0], l[1], l[2], l[3]);
+          }
         }
       }
       if (GRAD) {
@@ -388,7 +451,13 @@ __global__ void __launch_bounds__(NR, NR == 128 ? 4 : 1) lu_tc_kernel(Job<float>
       umma::fence_proxy_async_smem();
       tc_sync();
       FX_TOC(tq, 3);
-      if (GRAD || k0 + kw < n) {
+      if (IEEE) {
+        // the rows that the update changes: every row in gradient mode, the unpivoted ones in
+        // the forward (whose coefficients of pivoted rows are zero); the forward's columns
+        // before the panel's end stay as they are (B is zero there)
+        if ((GRAD || k0 + kw < n) && __any_sync(0xffffffffu, x < n && (GRAD || mypos < 0)))
+          lu_tc_fma_update<NR>(lu_tc_brow<NR>(S), trow, n, GRAD ? 0 : k0 + kw, c);
+      } else if (GRAD || k0 + kw < n) {
         if (tid == 0) {
           const uint32_t idesc = umma::idesc_tf32(128, NR, true);  // D -= C B^T, M = 128, N = NR
 #pragma unroll
