@@ -1,5 +1,6 @@
-// Tensor-memory resident Gauss-Jordan LU for float32 slogdet, 8 <= n <= 256,
-// prec = "tf32x3": forward (sign, logabs) and, in the same pass, A^-1 for the gradient.
+// Tensor-memory resident Gauss-Jordan LU for float32 slogdet, 8 <= n <= 256: forward
+// (sign, logabs) and, in the same pass, A^-1 for the gradient; prec = "tf32x3" (tensor-core
+// block updates) or "ieee" (IEEE float32 FMA block updates, template flag IEEE).
 //
 // Reference behaviour: LU with partial pivoting (largest |entry| of the current column
 // among the rows not yet pivoted, first occurrence on ties) as in src/fermix/_lu.py:51-120

@@ -1,5 +1,6 @@
-// Tensor-memory resident Parlett-Reid "sweep" for float32 slogpf, 8 <= n <= 128,
-// prec = "tf32x3": forward (sign, logabs) and, in the same pass, S^-1 for the gradient.
+// Tensor-memory resident Parlett-Reid "sweep" for float32 slogpf, 8 <= n <= 128: forward
+// (sign, logabs) and, in the same pass, S^-1 for the gradient; prec = "tf32x3" (tensor-core
+// block updates) or "ieee" (IEEE float32 FMA block updates, template flag IEEE).
 //
 // Reference behaviour: the pair steps and pivoting of src/fermix/_fallback.py:266-300
 // (pivot = largest corrected entry of column a among the unassigned rows, d = S[a, p]),
@@ -28,6 +29,11 @@
 // every thread solves z W_P = (its W row, or e_k on pivot row k) while the tensor core
 // runs the update, the pivot rows' new rows are the other rows' z transposed through
 // shared memory, and their pivot block is formed from the pivot rows' Z.
+//
+// Memory. With skew_symmetrize the matrix arrives through shared memory in 32-row chunks
+// (bulk copies, read once); the gradient leaves through per-warp shared-memory blocks as
+// whole 128-byte row pieces. Nothing is prefetched into L2 ahead of the block's next matrix:
+// the gradient writes evicted such lines before use, and the input was read twice.
 #pragma once
 #include "fused_lu.cuh"
 #include "tc_common.cuh"

@@ -177,7 +177,8 @@ __device__ __forceinline__ void tc_store_rows(float* __restrict__ dst, int n, fl
 // As tc_store_rows for a 16-byte aligned dst and n % 4 == 0, through this warp's 32 x 36 float
 // block of shared memory (wsm): each lane parks its 32 values of a column chunk as 16-byte
 // stores (conflict-free quarter-warps), then every warp store writes 4 whole 128-byte row
-// pieces, so the L2 receives whole 32-byte sectors instead of halves it might fill from DRAM.
+// pieces instead of 32 separate 16-byte pieces of 32 rows (fewer L2 write transactions;
+// measured faster for the gradient kernels).
 __device__ __forceinline__ void tc_store_rows_staged(float* __restrict__ dst, int n, float f, bool zero_out,
                                                      uint32_t trow, int x, float* __restrict__ wsm) {
   const int lane = x & 31, r0 = x - lane;
