@@ -79,3 +79,26 @@ def test_ieee_gather_matches_materialised():
     s1, l1 = host(fx.slogdet_gather(P, O, prec="ieee"))
     s2, l2 = host(fx.slogdet(cuda(phi[occ]), prec="ieee"))
     assert np.array_equal(s1, s2) and np.array_equal(l1, l2)
+
+
+@pytest.mark.parametrize("n,B", [(128, 1500), (256, 400)])
+def test_ieee_several_matrices_per_block(n, B):
+    """More matrices than resident blocks (592 at n <= 128, 148 at n = 256): each block walks
+    several members in turn. Forward and gradient against float64, per member."""
+    g = torch.Generator(device="cuda").manual_seed(800 + n)
+    A = torch.randn(B, n, n, device="cuda", generator=g)
+    s, l, G = fx.slogdet_parts(A, prec="ieee")
+    A64 = A.double()
+    s64, l64 = torch.linalg.slogdet(A64)
+    assert torch.equal(s.double(), s64)
+    err = (l.double() - l64).abs()
+    eps = np.finfo(np.float32).eps
+    over = torch.nonzero(err > 1e-4 * l64.abs().clamp(min=1)).flatten()
+    if over.numel():
+        cond = torch.linalg.cond(A64[over])
+        assert bool((err[over] <= 2 * cond * eps).all())
+    R = torch.linalg.inv(A64[:64]).transpose(-1, -2)
+    for i in range(64):
+        rel = float((G[i].double() - R[i]).abs().max() / R[i].abs().max())
+        cond = float(torch.linalg.cond(A64[i]))
+        assert rel <= max(1e-3, cond * eps), (i, rel, cond)
