@@ -34,14 +34,14 @@ TC_KERNEL = {"slogpf": "pf_tc_kernel", "slogdet": "lu_tc_kernel"}
 
 def kernel_name(a):
     """The dominant kernel of this workload: the tensor-memory kernels for float32 (slogpf
-    8 <= n <= 128, even n, both precisions: tcgen05 block updates under tf32x3, FMA ones
-    under ieee; slogdet 8 <= n <= 256 under tf32x3), the register-panel kernels otherwise up
-    to n = 256, and above that the blocked engines' trailing update (tcgen05 for float32 /
-    complex64 under tf32x3, DMMA for complex128, FMA tiles otherwise)."""
+    8 <= n <= 128, even n; slogdet 8 <= n <= 256; both precisions: tcgen05 block updates
+    under tf32x3, FMA ones under ieee), the register-panel kernels otherwise up to n = 256,
+    and above that the blocked engines' trailing update (tcgen05 for float32 / complex64
+    under tf32x3, DMMA for complex128, FMA tiles otherwise)."""
     if a.dtype == "f32" and a.n >= 8:
         if a.op == "slogpf" and a.n <= 128 and a.n % 2 == 0:
             return TC_KERNEL[a.op]
-        if a.op == "slogdet" and a.n <= 256 and a.prec == "tf32x3":
+        if a.op == "slogdet" and a.n <= 256:
             return TC_KERNEL[a.op]
     if a.n <= 256:
         return SMALL_KERNEL[a.op]
